@@ -1,0 +1,80 @@
+// Shared device helpers and the launch/status plumbing of the kernel ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "accel_b200.h"
+#include "status.h"
+
+namespace accel_b200 {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kSms = 148;  // B200: 2 dies x 74 SMs
+
+// ---------------------------------------------------------------- host side
+
+inline cudaStream_t AsStream(void* s) { return static_cast<cudaStream_t>(s); }
+
+inline int64_t CeilDiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+__host__ __device__ __forceinline__ int64_t Min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t Max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// ---------------------------------------------------------------- device side
+
+__device__ __forceinline__ float WarpSum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double WarpSum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float WarpMax(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// Exact Gelu of the reference (sim_device.cc:239): 0.5 * x * (1 + erf(x / sqrt 2)),
+// every step a rounded float operation.
+__device__ __forceinline__ float GeluExact(float v) {
+  const float e = erff(__fmul_rn(v, 0.7071067811865476f));
+  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.f, e));
+}
+
+// Epilogue of a product (include/accel_b200.h, accel_b200_epilogue), applied to
+// one output element: act(alpha * acc + beta * bias) + residual, each step a
+// rounded float operation as in sim_device.cc:227-241 and runtime.cc:336-344.
+struct Epilogue {
+  float alpha = 1.f;
+  float beta = 0.f;
+  const float* bias = nullptr;
+  int64_t bias_rs = 0;
+  int64_t bias_cs = 0;
+  int32_t act = 0;
+  const float* residual = nullptr;
+  int64_t residual_ld = 0;
+};
+
+__device__ __forceinline__ float ApplyEpilogue(const Epilogue& ep, float acc, int64_t i, int64_t j) {
+  float v = __fmul_rn(ep.alpha, acc);
+  if (ep.bias != nullptr) v = __fadd_rn(v, __fmul_rn(ep.beta, ep.bias[i * ep.bias_rs + j * ep.bias_cs]));
+  if (ep.act == ACCEL_B200_ACT_RELU) {
+    if (v < 0.f) v = 0.f;
+  } else if (ep.act == ACCEL_B200_ACT_GELU) {
+    v = GeluExact(v);
+  }
+  if (ep.residual != nullptr) v = __fadd_rn(v, ep.residual[i * ep.residual_ld + j]);
+  return v;
+}
+
+}  // namespace accel_b200

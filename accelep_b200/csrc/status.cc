@@ -1,0 +1,43 @@
+// Error and launch bookkeeping shared by every C entry point of the library.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <string>
+
+#include "accel_b200.h"
+#include "status.h"
+
+namespace accel_b200 {
+namespace {
+thread_local std::string g_error;
+std::atomic<int64_t> g_launches{0};
+}  // namespace
+
+int SetError(int code, const std::string& message) {
+  g_error = message;
+  return code;
+}
+
+int ClearError() {
+  g_error.clear();
+  return ACCEL_B200_OK;
+}
+
+void NoteLaunches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int CheckLaunch(const char* what) {
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    return SetError(ACCEL_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(err));
+  }
+  NoteLaunches(1);
+  return ACCEL_B200_OK;
+}
+
+}  // namespace accel_b200
+
+extern "C" ACCEL_B200_API const char* accel_b200_last_error(void) { return accel_b200::g_error.c_str(); }
+
+extern "C" ACCEL_B200_API int64_t accel_b200_launch_count(void) {
+  return accel_b200::g_launches.load(std::memory_order_relaxed);
+}

@@ -1,0 +1,181 @@
+"""Calls into the kernel C ABI with torch CUDA tensors.
+
+torch only provides device memory and the current stream here; every
+computation is one of the library's kernels. Used by the parity tests and
+the benchmark.
+"""
+
+import ctypes
+
+import torch
+
+from ._lib import P_i64, Epilogue, Q8Plane, check, load
+
+ACT = {"none": 0, "relu": 1, "gelu": 2}
+
+
+def _s(stream=None):
+    return ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
+
+
+def _p(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def embed(ids, table, seq, id_offset=0, status=None):
+    hidden = table.shape[1]
+    out = torch.zeros(seq, hidden, dtype=torch.float32, device=table.device)
+    check(load().accel_b200_embed(_p(ids), id_offset, _p(table), _p(out), seq, hidden, table.shape[0], _p(status), _s()))
+    return out
+
+
+def rmsnorm(x, w, rows, dim, eps, row_offset=0):
+    y = torch.zeros(rows, dim, dtype=torch.float32, device=x.device)
+    check(load().accel_b200_rmsnorm(_p(x), _p(w), _p(y), rows, dim, eps, row_offset, _s()))
+    return y
+
+
+def rope(states, cos_t, sin_t, seq, n_heads, head_dim, position):
+    check(load().accel_b200_rope(_p(states), _p(cos_t), _p(sin_t), seq, n_heads, head_dim, position, _s()))
+    return states
+
+
+def append_cache(src, cache, seq, position, n_heads, head_dim):
+    check(load().accel_b200_append_cache(_p(src), _p(cache), seq, position, n_heads, head_dim, _s()))
+    return cache
+
+
+def attention(q, k, v, seq, position, heads, kv_heads, head_dim):
+    out = torch.zeros(seq, heads, head_dim, dtype=torch.float32, device=q.device)
+    check(load().accel_b200_attention(_p(q), _p(k), _p(v), _p(out), seq, position, heads, kv_heads, head_dim, _s()))
+    return out
+
+
+def silu_mul(gate, up):
+    check(load().accel_b200_silu_mul(_p(gate), _p(up), gate.numel(), _s()))
+    return gate
+
+
+def residual_add(dest, extra):
+    check(load().accel_b200_residual_add(_p(dest), _p(extra), dest.numel(), _s()))
+    return dest
+
+
+def sample(logits, vocab, temperature, rng_state, top_k, chosen=None, index=0):
+    chosen = chosen if chosen is not None else torch.full((index + 1,), -1, dtype=torch.int32, device=logits.device)
+    check(load().accel_b200_sample(_p(logits), _p(chosen), index, vocab, temperature, _p(rng_state), top_k, _s()))
+    return chosen
+
+
+def argmax_rows(logits):
+    rows, vocab = logits.shape
+    chosen = torch.full((rows,), -1, dtype=torch.int32, device=logits.device)
+    check(load().accel_b200_argmax_rows(_p(logits), rows, vocab, logits.stride(0), _p(chosen), 1, 0, _s()))
+    return chosen
+
+
+def sample_rows(logits, temperature, rng_states, top_k):
+    rows, vocab = logits.shape
+    chosen = torch.full((rows,), -1, dtype=torch.int32, device=logits.device)
+    check(load().accel_b200_sample_rows(_p(logits), rows, vocab, logits.stride(0), _p(chosen), 1, 0, temperature,
+                                        _p(rng_states), top_k, _s()))
+    return chosen
+
+
+def matmul_exact(a, b):
+    m, k = a.shape
+    n = b.shape[1]
+    c = torch.full((m, n), 7.0, dtype=torch.float32, device=a.device)
+    check(load().accel_b200_matmul(_p(a), _p(b), _p(c), m, k, n, _s()))
+    return c
+
+
+def transpose(src):
+    rows, cols = src.shape
+    dst = torch.zeros(cols, rows, dtype=torch.float32, device=src.device)
+    check(load().accel_b200_transpose(_p(src), _p(dst), rows, cols, _s()))
+    return dst
+
+
+def gemm_epilogue(c, alpha, bias, bias_shape, beta, act):
+    m, n = c.shape
+    shape = (ctypes.c_int64 * max(1, len(bias_shape)))(*bias_shape)
+    check(load().accel_b200_gemm_epilogue(_p(c), m, n, alpha, _p(bias), ctypes.cast(shape, P_i64),
+                                          len(bias_shape) if bias is not None else 0, beta, ACT[act], _s()))
+    return c
+
+
+def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none", residual=None):
+    ep = Epilogue()
+    ep.alpha, ep.beta = alpha, beta
+    ep.bias = 0 if bias is None else bias.data_ptr()
+    ep.bias_row_stride, ep.bias_col_stride = bias_strides
+    ep.act = ACT[act]
+    ep.residual = 0 if residual is None else residual.data_ptr()
+    ep.residual_ld = 0 if residual is None else residual.stride(0)
+    return ep
+
+
+class Workspace:
+    """Grows a device byte buffer on demand."""
+
+    def __init__(self, device="cuda"):
+        self.device = device
+        self.buf = None
+
+    def get(self, nbytes):
+        if nbytes == 0:
+            return None
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+_WS = {}
+
+
+def _workspace(device, nbytes):
+    ws = _WS.setdefault(str(device), Workspace(device))
+    return ws.get(nbytes)
+
+
+def matmul_q8(a, q, scale, zero=None, axis=1, epilogue=None, out=None, offset=0, workspace=None):
+    """a [m, k] fp32, q int8 holding a [k, n] plane (at `offset`)."""
+    lib = load()
+    m, k = a.shape
+    n = q.shape[-1]
+    c = out if out is not None else torch.zeros(m, n, dtype=torch.float32, device=a.device)
+    plane = Q8Plane(q.data_ptr(), scale.data_ptr(), 0 if zero is None else zero.data_ptr(), offset, axis)
+    need = lib.accel_b200_matmul_q8_workspace(m, k, n)
+    ws = workspace if workspace is not None else _workspace(a.device, need)
+    check(lib.accel_b200_matmul_q8(_p(a), a.stride(0), ctypes.byref(plane), _p(c), c.stride(0), m, k, n,
+                                   None if epilogue is None else ctypes.byref(epilogue), _p(ws),
+                                   0 if ws is None else ws.numel(), _s()))
+    return c
+
+
+def matmul_f32(a, b, epilogue=None, out=None):
+    lib = load()
+    m, k = a.shape
+    n = b.shape[1]
+    c = out if out is not None else torch.zeros(m, n, dtype=torch.float32, device=a.device)
+    need = lib.accel_b200_matmul_f32_workspace(m, k, n)
+    ws = _workspace(a.device, need)
+    check(lib.accel_b200_matmul_f32(_p(a), a.stride(0), _p(b), _p(c), c.stride(0), m, k, n,
+                                    None if epilogue is None else ctypes.byref(epilogue), _p(ws),
+                                    0 if ws is None else ws.numel(), _s()))
+    return c
+
+
+def attention_decode(q, k_cache, v_cache, lens, heads, kv_heads, head_dim, max_len, chunk=256):
+    """q [B, heads * head_dim]; caches [B, max_len, kv_heads, head_dim]."""
+    lib = load()
+    batch = q.shape[0]
+    out = torch.zeros(batch, heads * head_dim, dtype=torch.float32, device=q.device)
+    need = lib.accel_b200_attention_decode_workspace(batch, heads, max_len, chunk)
+    ws = _workspace(q.device, need)
+    kvd = kv_heads * head_dim
+    check(lib.accel_b200_attention_decode(_p(q), q.stride(0), _p(k_cache), _p(v_cache), kvd, max_len * kvd, _p(lens),
+                                          batch, heads, kv_heads, head_dim, max_len, chunk, _p(out), out.stride(0),
+                                          _p(ws), ws.numel(), _s()))
+    return out

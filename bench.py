@@ -1,0 +1,313 @@
+"""Decode throughput of the int8 SmolLM2-135M-shaped Llama on B200.
+
+Workload (C4): 32 independent sequences per GPU, prompts of 512 uniform
+random ids, decoded greedily to a 2048 context (1536 new ids each), through
+the Llama C API (accel_llama_generate_batch). One step = one whole job:
+prefill of the 32 prompts plus the 1536-token decode loop. Weights are
+random-init (std 0.02, seeded) quantized per output row to int8; inputs are
+synthetic. N GPUs run N independent replicas, each with its own 32
+sequences (weak scaling, no data-path collective).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints one JSON line. `--impl reference` times the AccelEP reference's own
+CPU path (oracle/_ref, compiled from its sources) on the host cores.
+"""
+
+import argparse
+import ctypes
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from accelep_b200 import synthetic as syn  # noqa: E402
+
+METRIC = "decode tok/s (SmolLM2-shape, int8 W)"
+UNIT = "tok/s"
+SEQS = 32
+PROMPT = 512
+CONTEXT = 2048
+NEW = CONTEXT - PROMPT
+WEIGHT_SEED = 4
+PROMPT_SEED = 41
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM = 6650.0
+
+
+def config(n):
+    return {"workload": "C4: SmolLM2-135M shape, int8 per-row weights, 32 seqs/GPU x 512-token prompts, greedy "
+                        "decode to 2048 context (1536 new ids per seq); one step = prefill + whole decode",
+            "model": "SmolLM2-135M-shaped Llama (30 layers, hidden 576, 9/3 heads, inter 1536, vocab 49152)",
+            "global_batch": SEQS * n, "seq_len": CONTEXT, "prompt_len": PROMPT, "new_tokens_per_seq": NEW,
+            "parallelism": f"replicas x{n} (independent sequences, no collective)",
+            "l2": "inputs larger than L2: KV cache 3.0 GB and 135 MB of int8 weights per step"}
+
+
+def hbm_peak():
+    try:
+        peaks = json.loads(PEAKS.read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[3:7]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU baseline
+
+def _cpu_worker(args):
+    """One single-threaded reference process: the C4 model (dequantized int8
+    weights, which is the reference's int8 arithmetic) generating `new` ids
+    after a short prompt. Returns (ids, seconds)."""
+    index, prompt_len, new = args
+    sys.path.insert(0, str(ROOT))
+    from oracle.oracle import LlamaHandle, Reference
+
+    cfg = dict(syn.SMOLLM2_135M, context=prompt_len + new + 1)
+    _, dense = syn.llama_int8(cfg, WEIGHT_SEED)
+    model = LlamaHandle(Reference(), cfg)
+    model.load(dense)
+    del dense
+    prompt = syn.prompts(syn.SMOLLM2_135M, SEQS, PROMPT, PROMPT_SEED)[index % SEQS][:prompt_len]
+    t0 = time.perf_counter()
+    ids = model.generate(prompt, new)
+    return len(ids), time.perf_counter() - t0
+
+
+def reference_throughput(workers, prompt_len=8, new=24):
+    """Aggregate decode tok/s of `workers` reference processes running at once."""
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers) as pool:
+        t0 = time.perf_counter()
+        results = pool.map(_cpu_worker, [(i, prompt_len, new) for i in range(workers)])
+        wall = time.perf_counter() - t0
+    tokens = sum(r[0] for r in results)
+    per_proc = max(r[1] for r in results)
+    return tokens / per_proc, tokens, per_proc, wall
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    workers = max(1, min(SEQS, cores))
+    sample = (f"{workers} concurrent single-threaded reference processes (oracle/_ref, compiled from the AccelEP "
+              f"sources), each generating 24 greedy ids after an 8-token prompt on the C4 model (dequantized int8 "
+              f"weights); tok/s = all ids / slowest process time")
+    for _ in range(args.warmup):
+        reference_throughput(workers)
+    vals = []
+    t_all = time.perf_counter()
+    for _ in range(args.steps):
+        v, _, _, _ = reference_throughput(workers)
+        vals.append(v)
+    elapsed = time.perf_counter() - t_all
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / max(1, args.steps),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 weights dequantized)",
+            "data": "synthetic", "config": config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ B200 arm
+
+def attention_roofline(torch, stream, batch=SEQS, length=1280, reps=50):
+    """Times the split-KV decode attention launch alone at the workload's mean
+    context (1280 rows) with CUDA events on the launching stream; returns
+    (algorithmic GB/s, seconds per launch, bytes per launch)."""
+    from accelep_b200 import kernels as K
+
+    cfg = syn.SMOLLM2_135M
+    heads, kvh, hd = cfg["heads"], cfg["kv_heads"], cfg["hidden"] // cfg["heads"]
+    kvd = kvh * hd
+    with torch.cuda.stream(stream):
+        # Several cache copies rotated so each launch reads from HBM, not L2.
+        copies = 4
+        kc = [torch.randn(batch, CONTEXT, kvh, hd, device="cuda") for _ in range(copies)]
+        vc = [torch.randn(batch, CONTEXT, kvh, hd, device="cuda") for _ in range(copies)]
+        q = torch.randn(batch, heads * hd, device="cuda")
+        lens = torch.full((batch,), length, dtype=torch.int32, device="cuda")
+        for i in range(3):
+            K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kvh, hd, CONTEXT)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(reps):
+            K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kvh, hd, CONTEXT)
+        end.record(stream)
+        end.synchronize()
+    sec = start.elapsed_time(end) / 1000.0 / reps
+    nbytes = batch * length * 2 * kvd * 4 + 2 * batch * heads * hd * 4
+    del kc, vc
+    return nbytes / sec / 1e9, sec, nbytes
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+
+    from accelep_b200 import load
+    from accelep_b200.llama import Llama
+
+    lib = load()
+    cfg = syn.SMOLLM2_135M
+    planes, dense = syn.llama_int8(cfg, WEIGHT_SEED)
+    model = Llama(cfg)
+    model.load_int8(planes, dense)
+    del planes, dense
+    prompts = list(syn.prompts(cfg, SEQS, PROMPT, PROMPT_SEED))
+    stream = torch.cuda.ExternalStream(model.stream())
+
+    def step():
+        return model.generate_batch(prompts, NEW)
+
+    for _ in range(max(3, args.warmup)):
+        out = step()
+    assert all(len(o) == NEW for o in out)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    launches0 = lib.accel_b200_launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = step()
+    end.record(stream)
+    end.synchronize()
+    wall = time.perf_counter() - t0
+    barrier()
+    launches = lib.accel_b200_launch_count() - launches0
+    clk = clocks.stop()
+    dev_sec = start.elapsed_time(end) / 1000.0
+    tensor = torch.tensor([dev_sec, wall], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(tensor, op=dist.ReduceOp.MAX)
+    dev_sec, wall = float(tensor[0]), float(tensor[1])
+    tokens = SEQS * NEW * world * args.steps
+    value = tokens / dev_sec
+
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        achieved, sec, nbytes = attention_roofline(torch, stream)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cores = 1
+            v, toks, per, _ = reference_throughput(1, prompt_len=8, new=48)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "reference",
+                   "sample": f"one single-threaded reference process (oracle/_ref), {toks} greedy ids after an "
+                             f"8-token prompt on the C4 model (dequantized int8 weights) in {per:.1f} s"}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(3, args.warmup), "ms_per_step": 1000.0 * dev_sec / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 compute",
+                "data": "synthetic (seeded random-init weights and prompts)", "config": config(world),
+                "e2e": {"value": tokens / wall, "unit": UNIT, "h2d_bytes_per_step": SEQS * PROMPT * 4,
+                        "d2h_bytes_per_step": SEQS * NEW * 4},
+                "gpu_launches": int(launches),
+                "roofline": {"kernel": "attention_decode (split-KV, B=32, 1280 context rows)", "bound": "hbm",
+                             "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None,
+                             "bytes_per_launch": nbytes, "us_per_launch": sec * 1e6},
+                "cpu_baseline": cpu, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,253 @@
+/*
+ * accel_b200.h: the C ABI of the B200 kernels behind AccelEP's device calls.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL is the legacy default stream) and
+ * returns 0 or a nonzero ACCEL_B200_E* status. The message of the last
+ * failure on the calling thread is in accel_b200_last_error(). Launches are
+ * asynchronous: a status of 0 means the launch was accepted, and an error a
+ * kernel detects on the device (for example a token id outside the
+ * vocabulary) is raised through a device status word the caller passes.
+ *
+ * Each entry point replaces one routine of the reference SimDevice; the
+ * citation names the reference file and line (paths relative to the AccelEP
+ * project root). Floating-point results agree with the reference within
+ * rtol = atol = 1e-4; index, copy and integer results are bit-identical.
+ * Entry points marked "bit-exact" also round every floating-point step where
+ * the reference does and so give the reference's bits.
+ */
+#ifndef ACCEL_B200_H_
+#define ACCEL_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define ACCEL_B200_API __declspec(dllexport)
+#else
+#define ACCEL_B200_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ACCEL_B200_OK = 0,
+  ACCEL_B200_EINVAL = 1,    /* argument out of range: std::invalid_argument in the reference */
+  ACCEL_B200_EOVERFLOW = 2, /* size arithmetic overflows: std::overflow_error in the reference */
+  ACCEL_B200_ECUDA = 3,     /* a CUDA runtime call failed */
+  ACCEL_B200_EDEVICE = 4,   /* a kernel reported an error through its status word */
+  ACCEL_B200_ENOMEM = 5     /* an allocation failed: std::bad_alloc in the reference */
+};
+
+/* Activation codes: include/accel/device.h:11 (Activation::None/Relu/Gelu). */
+enum { ACCEL_B200_ACT_NONE = 0, ACCEL_B200_ACT_RELU = 1, ACCEL_B200_ACT_GELU = 2 };
+
+/* Bits of a device status word written by kernels that validate data. */
+enum { ACCEL_B200_STATUS_BAD_TOKEN = 1 };
+
+ACCEL_B200_API const char* accel_b200_last_error(void);
+/* Number of kernel launches this library has issued in this process
+   (each replayed graph node counts once per replay). */
+ACCEL_B200_API int64_t accel_b200_launch_count(void);
+
+/* ---------------------------------------------------------- named kernels */
+
+/* src/sim_embed.cc:9-20. out[s, :] = table[ids[id_offset + s], :]. An id
+   outside [0, vocab) leaves its row untouched and ORs
+   ACCEL_B200_STATUS_BAD_TOKEN into *status (device int; may be NULL).
+   Bit-exact. */
+ACCEL_B200_API int accel_b200_embed(const int32_t* ids, int64_t id_offset, const float* table, float* out, int64_t seq,
+                                    int64_t hidden, int64_t vocab, int32_t* status, void* stream);
+
+/* src/sim_rmsnorm.cc:7-20. y[r, :] = float(x[row_offset + r, :] * inv) * w with the
+   sum of squares and inv in double. */
+ACCEL_B200_API int accel_b200_rmsnorm(const float* x, const float* weight, float* y, int64_t rows, int64_t dim,
+                                      float eps, int64_t row_offset, void* stream);
+
+/* src/sim_rope.cc:5-21. In-place rotate-half RoPE on [seq, n_heads, head_dim]
+   with table rows at absolute positions position + s. Bit-exact. */
+ACCEL_B200_API int accel_b200_rope(float* states, const float* cos_table, const float* sin_table, int64_t seq,
+                                   int64_t n_heads, int64_t head_dim, int64_t position, void* stream);
+
+/* src/sim_cache.cc:8-13. Copies seq rows of n_heads * head_dim floats into
+   cache rows [position, position + seq). Bit-exact. */
+ACCEL_B200_API int accel_b200_append_cache(const float* src, float* cache, int64_t seq, int64_t position,
+                                           int64_t n_heads, int64_t head_dim, void* stream);
+
+/* src/sim_attend.cc:9-46. Causal grouped-query attention. q and out are
+   [seq, heads, head_dim]; k and v hold rows [0, position + seq) of
+   [rows, kv_heads, head_dim]. heads must be a multiple of kv_heads. The
+   reference's `scores` scratch is not needed. */
+ACCEL_B200_API int accel_b200_attention(const float* q, const float* k, const float* v, float* out, int64_t seq,
+                                        int64_t position, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                        void* stream);
+
+/* src/sim_silu.cc:8-13. gate[i] = gate[i] / (1 + exp(-gate[i])) * up[i]. */
+ACCEL_B200_API int accel_b200_silu_mul(float* gate, const float* up, int64_t count, void* stream);
+
+/* src/sim_add.cc:5-9. dest[i] += extra[i]. Bit-exact. */
+ACCEL_B200_API int accel_b200_residual_add(float* dest, const float* extra, int64_t count, void* stream);
+
+/* src/sim_sample.cc:25-115. Writes one int32 at chosen[chosen_index].
+   temperature <= 0: argmax, the earlier id wins a tie (bit-exact). Otherwise
+   top-k (at most 64 logits, walked in id order) or the whole vocabulary,
+   with one xorshift32 draw from *rng_state (a device uint32, advanced in
+   place like the reference's host state). */
+ACCEL_B200_API int accel_b200_sample(const float* logits, int32_t* chosen, int64_t chosen_index, int64_t vocab,
+                                     float temperature, uint32_t* rng_state, int32_t top_k, void* stream);
+
+/* Greedy choice for `rows` logit rows of row stride ld: chosen[r * chosen_stride
+   + chosen_offset] = argmax(logits[r, :]). Same tie and NaN rules as
+   accel_b200_sample at temperature 0 (batched form of src/sim_sample.cc:27-38). */
+ACCEL_B200_API int accel_b200_argmax_rows(const float* logits, int64_t rows, int64_t vocab, int64_t ld, int32_t* chosen,
+                                          int64_t chosen_stride, int64_t chosen_offset, void* stream);
+
+/* ---------------------------------------------------------------- matrices */
+
+/* src/sim_device.cc:185-196 (MatMul -> PackedMatMul :331-369). Row-major
+   C[m, n] = A[m, k] @ B[k, n], each output a k-ascending chain of rounded
+   products and rounded adds, as the reference computes it. Bit-exact. */
+ACCEL_B200_API int accel_b200_matmul(const float* a, const float* b, float* c, int64_t m, int64_t k, int64_t n,
+                                     void* stream);
+
+/* src/sim_device.cc:198-209. dst[j, i] = src[i, j]; src is [rows, cols]. Bit-exact. */
+ACCEL_B200_API int accel_b200_transpose(const float* src, float* dst, int64_t rows, int64_t cols, void* stream);
+
+/* src/sim_device.cc:211-245 with BiasOffset :104-124.
+   c = act(alpha * c + beta * broadcast(bias)); bias may be NULL; bias_shape
+   (rank 0..2) is right-aligned against [m, n] with size-1 axes broadcast.
+   Relu keeps NaN and -0; Gelu is 0.5 x (1 + erf(x / sqrt 2)). */
+ACCEL_B200_API int accel_b200_gemm_epilogue(float* c, int64_t m, int64_t n, float alpha, const float* bias,
+                                            const int64_t* bias_shape, int32_t bias_rank, float beta, int32_t act,
+                                            void* stream);
+
+/* An int8 weight plane (include/accel/runtime.h:71-78, QuantPlane) holding B
+   of a [k, n] product. The element at (kk, j) is q[offset + kk * n + j] and
+   dequantizes to (float(q) - zero) * scale, with scale and zero indexed by the
+   plane's `axis` coordinate of a [k, n] tensor (axis 0: per row kk, axis 1:
+   per column j, -1: one value). `zero` may be NULL. */
+typedef struct accel_b200_q8_plane {
+  const int8_t* q;
+  const float* scale;
+  const int8_t* zero;
+  int64_t offset;
+  int32_t axis;
+} accel_b200_q8_plane;
+
+/* Output stage fused into a product (src/runtime.cc:332-344 and
+   sim_device.cc:211-245): out = act(alpha * acc + beta * bias) + residual.
+   bias is NULL or broadcast by (bias_row_stride, bias_col_stride) in floats
+   (0 for a broadcast axis); residual is NULL or [m, n] with row stride
+   residual_ld. residual may alias the output. */
+typedef struct accel_b200_epilogue {
+  float alpha;
+  float beta;
+  const float* bias;
+  int64_t bias_row_stride;
+  int64_t bias_col_stride;
+  int32_t act;
+  const float* residual;
+  int64_t residual_ld;
+} accel_b200_epilogue;
+
+/* Scratch, in bytes, accel_b200_matmul_q8 needs for these sizes (0 when the
+   product runs in one pass). */
+ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64_t n);
+
+/* src/sim_device.cc:541-602 (MatMulQuantized with a right-hand plane) and
+   the epilogue the runtime applies after it (src/runtime.cc:326-344):
+   c[m, n] = epilogue(A[m, k] @ dequant(B)), with A fp32 row-major (row
+   stride lda) and C row stride ldc. ep may be NULL (plain product).
+   workspace must hold accel_b200_matmul_q8_workspace(m, k, n) bytes (it may
+   be NULL when that is 0); concurrent calls need separate workspaces. */
+ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c,
+                                        int64_t ldc, int64_t m, int64_t k, int64_t n,
+                                        const accel_b200_epilogue* ep, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
+/* fp32 weights with the same fused epilogue and split-K scheme: the fast
+   (fused multiply-add, reassociated) product the Llama engine uses. */
+ACCEL_B200_API size_t accel_b200_matmul_f32_workspace(int64_t m, int64_t k, int64_t n);
+ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const float* b, float* c, int64_t ldc, int64_t m,
+                                         int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------- batched decode kernels
+   Fused forms of reference call sequences, used by the Llama engine
+   (src/llama_model.cc:209-247 and :101-131). Rows of one launch may belong
+   to different sequences: `row_seq[r]` is a row's sequence slot and
+   `row_pos[r]` its absolute position (-1: a finished sequence, skipped). */
+
+/* Rope on the query and key heads and AppendCache of key and value
+   (src/llama_model.cc:229-232) over fused projection rows
+   qkv[r] = [q (heads * head_dim) | k (kv_heads * head_dim) | v]. Queries are
+   rotated in place; keys and values land in cache row row_pos[r] of slot
+   row_seq[r] (row_seq may be NULL: slot 0). A cache slot is [context,
+   kv_heads, head_dim]; slots are cache_seq_stride floats apart. Bit-exact. */
+ACCEL_B200_API int accel_b200_rope_append(float* qkv, int64_t qkv_ld, const int32_t* row_seq, const int32_t* row_pos,
+                                          int64_t rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                          const float* cos_table, const float* sin_table, float* k_cache,
+                                          float* v_cache, int64_t cache_seq_stride, void* stream);
+
+/* Causal attention of each row over its own sequence's cache rows
+   [0, row_pos[r]] (src/sim_attend.cc:9-46 with per-row sequence and
+   position). q row r: q + r * q_row_stride; cache row t of slot s: k + s *
+   kv_seq_stride + t * kv_row_stride. */
+ACCEL_B200_API int accel_b200_attention_rows(const float* q, int64_t q_row_stride, const float* k, const float* v,
+                                             int64_t kv_row_stride, int64_t kv_seq_stride, float* out,
+                                             int64_t out_row_stride, const int32_t* row_seq, const int32_t* row_pos,
+                                             int64_t rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                             void* stream);
+
+/* Split-KV decode attention, head_dim 64: one query row per sequence b over
+   cache rows [0, lens[b]) of slot b (1 <= lens[b] <= max_len). Context chunks
+   of `chunk` rows are reduced in parallel into `workspace` and merged. */
+ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32_t heads, int32_t max_len,
+                                                            int32_t chunk);
+ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_stride, const float* k, const float* v,
+                                               int64_t kv_row_stride, int64_t kv_seq_stride, const int32_t* lens,
+                                               int32_t batch, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                               int32_t max_len, int32_t chunk, float* out, int64_t out_row_stride,
+                                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* SiluMul (src/sim_silu.cc:8-13) over fused rows [gate (inter) | up (inter)]
+   of row stride ld into out[r, i] (row stride ldo). */
+ACCEL_B200_API int accel_b200_silu_mul_rows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows,
+                                            int64_t inter, void* stream);
+
+/* Batched SampleToken (src/sim_sample.cc:25-115): row r draws with its own
+   device state rng_states[r] and writes chosen[r * chosen_stride +
+   chosen_offset]. */
+ACCEL_B200_API int accel_b200_sample_rows(const float* logits, int64_t rows, int64_t vocab, int64_t ld, int32_t* chosen,
+                                          int64_t chosen_stride, int64_t chosen_offset, float temperature,
+                                          uint32_t* rng_states, int32_t top_k, void* stream);
+
+/* One step of Generate's loop (src/llama_model.cc:113-128) for `batch`
+   sequences at once. Sequence b (unless done[b]): id = argmax(logits[b])
+   (or pre_ids[b] when pre_ids is not NULL); ids[b * ids_stride + step] = id;
+   count[b] = step + 1; then id == eos or lens[b] >= context ends it (done[b]
+   = 1, row_pos[b] = -1, *finished += 1), else tokens[b] = id, row_pos[b] =
+   lens[b], lens[b] += 1. step points to two device ints {step, 0}; the
+   launch advances step[0] by one, so it can be replayed from a graph. */
+ACCEL_B200_API int accel_b200_greedy_step(const float* logits, const int32_t* pre_ids, int64_t vocab, int64_t ld,
+                                          int32_t* ids, int64_t ids_stride, int32_t* count, int32_t* done,
+                                          int32_t* tokens, int32_t* row_pos, int32_t* lens, int32_t eos,
+                                          int32_t context, int32_t* step, int32_t* finished, int32_t batch,
+                                          void* stream);
+
+/* dst[r, :] = src[idx[r], :] for r < rows (cols floats per row): the last
+   prompt row of each sequence before the final norm (src/llama_model.cc:244). */
+ACCEL_B200_API int accel_b200_gather_rows(const float* src, int64_t ld, const int32_t* idx, int64_t rows, int64_t cols,
+                                          float* dst, int64_t ldd, void* stream);
+
+/* *out = max over i of |a[i] - b[i]|, NaN differences ignored: the logit
+   check of src/llama_model.cc:168-181 done on the device. */
+ACCEL_B200_API int accel_b200_max_abs_diff(const float* a, const float* b, int64_t n, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACCEL_B200_H_ */
