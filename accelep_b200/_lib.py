@@ -63,18 +63,19 @@ SIGNATURES = {
     "accel_b200_matmul_f32_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_f32": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_rope_append": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
-                                       c_i64, c_vp]),
-    "accel_b200_attention_rows": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
-                                          c_i32, c_i32, c_i32, c_vp]),
-    "accel_b200_attention_decode_workspace": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
-    "accel_b200_attention_decode": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32,
-                                            c_i32, c_i32, c_vp, c_i64, c_vp, c_sz, c_vp]),
+                                       c_i64, c_i64, c_i64, c_vp]),
+    "accel_b200_attention_rows": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp,
+                                          c_i64, c_i32, c_i32, c_i32, c_vp]),
+    "accel_b200_attention_decode_workspace": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "accel_b200_attention_decode": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32,
+                                            c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_sz, c_vp, c_vp]),
     "accel_b200_silu_mul_rows": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "accel_b200_sample_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_f32, c_vp, c_i32, c_vp]),
     "accel_b200_greedy_step": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32,
                                        c_i32, c_vp, c_vp, c_i32, c_vp]),
     "accel_b200_gather_rows": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "accel_b200_max_abs_diff": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp]),
+    "accel_b200_wait_selftest": (c_int, [c_vp, c_vp]),
     # The reference's one-matmul API.
     "accel_sim_create": (c_vp, []),
     "accel_sim_destroy": (None, [c_vp]),

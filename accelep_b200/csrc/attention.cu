@@ -5,12 +5,12 @@
 //    chunks of the context. Any head_dim up to 1024, any context length.
 //    It serves Device::Attention and prefill, where many query rows share
 //    each key row and the key rows stay in L2.
-//  * AttnDecodeKernel + AttnCombineKernel: split-KV ("flash decoding") for
-//    one new query row per sequence with head_dim 64. One CTA per
-//    (sequence, kv head, context chunk) reads each key and value row of its
-//    chunk once from HBM for all query heads that share the kv head, and
-//    writes a partial (max, sum, weighted values) that the combine kernel
-//    merges with the log-sum-exp rule.
+//  * AttnDecodeKernel: split-KV ("flash decoding") for one new query row per
+//    sequence with head_dim 64. One CTA per (sequence, kv head, context
+//    chunk) bulk-copies the chunk's key and value rows into shared memory
+//    once for all query heads that share the kv head, writes a partial
+//    (max, sum, weighted values), and the last CTA of the (sequence, kv head)
+//    merges the partials with the log-sum-exp rule.
 //
 // The reference divides each weight by the sum before the value product;
 // here the sum divides the accumulated product once. The two orders agree
@@ -21,6 +21,7 @@
 
 #include "accel_b200.h"
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace accel_b200 {
 namespace {
@@ -35,6 +36,7 @@ struct RowsArgs {
   const float* k;
   const float* v;
   int64_t kv_row_stride;
+  int64_t kv_head_stride;
   int64_t kv_seq_stride;
   float* out;
   int64_t out_row_stride;
@@ -81,8 +83,8 @@ __global__ void __launch_bounds__(kRowsThreads) AttnRowsKernel(RowsArgs a) {
   const int64_t seq = a.row_seq != nullptr ? a.row_seq[r] : 0;
   const int64_t limit = a.row_pos != nullptr ? a.row_pos[r] : a.position + r;
   const float* qrow = a.q + r * a.q_row_stride + static_cast<int64_t>(h) * D;
-  const float* kbase = a.k + seq * a.kv_seq_stride + static_cast<int64_t>(g) * D;
-  const float* vbase = a.v + seq * a.kv_seq_stride + static_cast<int64_t>(g) * D;
+  const float* kbase = a.k + seq * a.kv_seq_stride + static_cast<int64_t>(g) * a.kv_head_stride;
+  const float* vbase = a.v + seq * a.kv_seq_stride + static_cast<int64_t>(g) * a.kv_head_stride;
   for (int d = threadIdx.x; d < D; d += blockDim.x) q_s[d] = qrow[d];
   float acc[kMaxDPerThread];
 #pragma unroll
@@ -137,147 +139,177 @@ __global__ void __launch_bounds__(kRowsThreads) AttnRowsKernel(RowsArgs a) {
 constexpr int kDecD = 64;
 constexpr int kDecThreads = 128;
 constexpr int kMaxGroup = 8;
+constexpr int kPart = kDecD + 2;  // weighted values, max, sum
 
 struct DecodeArgs {
   const float* q;  // row b: heads * 64 floats at q + b * q_row_stride
   int64_t q_row_stride;
-  const float* k;  // sequence b, row t, kv head g: k + b * kv_seq_stride + t * kv_row_stride + g * 64
+  const float* k;  // slot b, kv head g, row t: k + b * seq + g * head + t * row (floats)
   const float* v;
   int64_t kv_row_stride;
+  int64_t kv_head_stride;
   int64_t kv_seq_stride;
   const int32_t* lens;  // context length of sequence b (new row included)
   int32_t heads;
   int32_t kv_heads;
-  int32_t chunk;      // context rows per CTA
-  int32_t n_chunks;   // grid.x
+  int32_t chunk;     // context rows per CTA
+  int32_t n_chunks;  // grid.x
   float scale;
-  float* part;  // [B][heads][n_chunks][kDecD + 2]: weighted values, max, sum
+  float* part;        // [B][heads][n_chunks][kPart]
+  int32_t* counters;  // [B][kv_heads]: arrivals; zero before and after a launch
+  int32_t* status;    // ORs ACCEL_B200_STATUS_COPY_TIMEOUT; may be null
+  float* out;
+  int64_t out_row_stride;
 };
 
+// One CTA per (chunk, kv head, sequence). The chunk's key and value rows are
+// pulled into shared memory by bulk copies (one copy per operand when rows
+// are contiguous, else one per row), the G query heads of the kv head score
+// them, and a partial (max, sum, weighted values) per head goes to the
+// workspace. The last CTA of a (sequence, kv head) to arrive merges the
+// partials in chunk order, so the result does not depend on arrival order.
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) AttnDecodeKernel(DecodeArgs a) {
-  extern __shared__ float smem[];
-  float* q_s = smem;                       // G * 64
-  float* p_s = smem + G * kDecD;           // G * chunk
-  float* red = p_s + G * a.chunk;          // 4 warps * G * 64 partial values
+  extern __shared__ __align__(128) float smem[];
+  const int C = a.chunk;
+  float* ks = smem;               // C * 64
+  float* vs = ks + C * kDecD;     // C * 64
+  float* qs = vs + C * kDecD;     // G * 64
+  float* ps = qs + G * kDecD;     // G * C
+  __shared__ __align__(8) uint64_t bar;
   __shared__ float stat[2 * kMaxGroup];
+  __shared__ int32_t last;
   const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t len = a.lens[b];
-  const int64_t t0 = static_cast<int64_t>(c) * a.chunk;
-  const int cnt = static_cast<int>(Max64(0, Min64(a.chunk, len - t0)));
+  const int64_t t0 = static_cast<int64_t>(c) * C;
+  const int cnt = static_cast<int>(Max64(0, Min64(C, len - t0)));
   const int h0 = g * G;
-  float* part_base = a.part + ((static_cast<int64_t>(b) * a.heads + h0) * a.n_chunks + c) * (kDecD + 2);
-  const int64_t part_head_stride = static_cast<int64_t>(a.n_chunks) * (kDecD + 2);
-  if (cnt == 0) {
-    for (int i = tid; i < G; i += blockDim.x) {
-      part_base[i * part_head_stride + kDecD] = -INFINITY;
-      part_base[i * part_head_stride + kDecD + 1] = 0.f;
+  const int64_t head_part = static_cast<int64_t>(a.n_chunks) * kPart;
+  float* part_base = a.part + ((static_cast<int64_t>(b) * a.heads + h0) * a.n_chunks + c) * kPart;
+
+  if (cnt > 0) {
+    const float* kb = a.k + b * a.kv_seq_stride + g * a.kv_head_stride + t0 * a.kv_row_stride;
+    const float* vb = a.v + b * a.kv_seq_stride + g * a.kv_head_stride + t0 * a.kv_row_stride;
+    const bool contiguous = a.kv_row_stride == kDecD;
+    if (tid == 0) {
+      MbarInit(&bar, 1);
+      FenceBarrierInit();
     }
-    return;
-  }
-  const float* qrow = a.q + static_cast<int64_t>(b) * a.q_row_stride + static_cast<int64_t>(h0) * kDecD;
-  for (int i = tid; i < G * kDecD; i += blockDim.x) q_s[i] = qrow[i];
-  __syncthreads();
-  const float* kb = a.k + static_cast<int64_t>(b) * a.kv_seq_stride + t0 * a.kv_row_stride + static_cast<int64_t>(g) * kDecD;
-  const float* vb = a.v + static_cast<int64_t>(b) * a.kv_seq_stride + t0 * a.kv_row_stride + static_cast<int64_t>(g) * kDecD;
-  // Scores: one key row per thread, 16-byte loads, all G heads per row.
-  for (int j = tid; j < cnt; j += blockDim.x) {
-    const float4* kr = reinterpret_cast<const float4*>(kb + j * a.kv_row_stride);
-    float dot[G];
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) dot[hh] = 0.f;
-#pragma unroll
-    for (int d4 = 0; d4 < kDecD / 4; ++d4) {
-      const float4 kv = __ldg(kr + d4);
-#pragma unroll
-      for (int hh = 0; hh < G; ++hh) {
-        // Every lane reads the same q words: a shared-memory broadcast.
-        const float* qh = q_s + hh * kDecD + d4 * 4;
-        dot[hh] = fmaf(qh[0], kv.x, dot[hh]);
-        dot[hh] = fmaf(qh[1], kv.y, dot[hh]);
-        dot[hh] = fmaf(qh[2], kv.z, dot[hh]);
-        dot[hh] = fmaf(qh[3], kv.w, dot[hh]);
+    __syncthreads();
+    if (tid == 0) {
+      MbarArriveExpectTx(&bar, static_cast<uint32_t>(cnt) * kDecD * 4 * 2);
+      if (contiguous) {
+        BulkCopyG2S(ks, kb, static_cast<uint32_t>(cnt) * kDecD * 4, &bar);
+        BulkCopyG2S(vs, vb, static_cast<uint32_t>(cnt) * kDecD * 4, &bar);
       }
     }
+    __syncthreads();  // the expected byte count is posted before row copies land
+    if (!contiguous) {
+      for (int j = tid; j < cnt; j += kDecThreads) {
+        BulkCopyG2S(ks + j * kDecD, kb + j * a.kv_row_stride, kDecD * 4, &bar);
+        BulkCopyG2S(vs + j * kDecD, vb + j * a.kv_row_stride, kDecD * 4, &bar);
+      }
+    }
+    const float* qrow = a.q + static_cast<int64_t>(b) * a.q_row_stride + static_cast<int64_t>(h0) * kDecD;
+    for (int i = tid; i < G * kDecD; i += kDecThreads) qs[i] = qrow[i];
+    __syncthreads();
+    bool ok = MbarWait(&bar, 0);
+    if (!ok) {
+      if (a.status != nullptr) atomicOr(a.status, ACCEL_B200_STATUS_COPY_TIMEOUT);
+      MbarWait(&bar, 0);  // give copies still in flight one more bounded wait
+    }
+    ok = __syncthreads_and(ok);
+    if (ok) {
+      // Scores: two threads per row, each over half of the dimensions; the
+      // float4 index rotates with the row so a quarter-warp hits 32 banks.
+      for (int base = 0; base < 2 * cnt; base += kDecThreads) {
+        const int task = base + tid;
+        const bool valid = task < 2 * cnt;  // uniform loop: every lane reaches the shuffle
+        const int j = valid ? task >> 1 : 0, half = task & 1;
+        float dot[G];
 #pragma unroll
-    for (int hh = 0; hh < G; ++hh) p_s[hh * a.chunk + j] = dot[hh] * a.scale;
+        for (int hh = 0; hh < G; ++hh) dot[hh] = 0.f;
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int d4 = half * 8 + ((i + j + 4 * half) & 7);
+            const float4 kv = *reinterpret_cast<const float4*>(ks + j * kDecD + d4 * 4);
+#pragma unroll
+            for (int hh = 0; hh < G; ++hh) {
+              const float4 qv = *reinterpret_cast<const float4*>(qs + hh * kDecD + d4 * 4);
+              dot[hh] = fmaf(qv.x, kv.x, dot[hh]);
+              dot[hh] = fmaf(qv.y, kv.y, dot[hh]);
+              dot[hh] = fmaf(qv.z, kv.z, dot[hh]);
+              dot[hh] = fmaf(qv.w, kv.w, dot[hh]);
+            }
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) {
+          const float other = __shfl_xor_sync(kFull, dot[hh], 1);
+          if (valid && half == 0) ps[hh * C + j] = (dot[hh] + other) * a.scale;
+        }
+      }
+      __syncthreads();
+      for (int hh = warp; hh < G; hh += kDecThreads / 32) {
+        float mx = -INFINITY;
+        for (int j = lane; j < cnt; j += 32) mx = fmaxf(mx, ps[hh * C + j]);
+        mx = WarpMax(mx);
+        float sum = 0.f;
+        for (int j = lane; j < cnt; j += 32) {
+          const float p = expf(ps[hh * C + j] - mx);
+          ps[hh * C + j] = p;
+          sum += p;
+        }
+        sum = WarpSum(sum);
+        if (lane == 0) {
+          stat[2 * hh] = mx;
+          stat[2 * hh + 1] = sum;
+        }
+      }
+      __syncthreads();
+      // Weighted values: thread owns dimension d for heads tid / 64, + 2, ...
+      const int d = tid & (kDecD - 1);
+      for (int hh = tid / kDecD; hh < G; hh += kDecThreads / kDecD) {
+        float acc = 0.f;
+        const float* p = ps + hh * C;
+        for (int j = 0; j < cnt; ++j) acc = fmaf(p[j], vs[j * kDecD + d], acc);
+        part_base[hh * head_part + d] = acc;
+      }
+      if (tid < G) {
+        part_base[tid * head_part + kDecD] = stat[2 * tid];
+        part_base[tid * head_part + kDecD + 1] = stat[2 * tid + 1];
+      }
+    } else if (tid < G) {
+      part_base[tid * head_part + kDecD] = -INFINITY;
+      part_base[tid * head_part + kDecD + 1] = 0.f;
+    }
   }
+  // Arrive; the last CTA of this (sequence, kv head) merges.
+  __threadfence();
   __syncthreads();
-  // Per head: max and exp-sum over the chunk; warp hh handles head hh.
-  for (int hh = warp; hh < G; hh += kDecThreads / 32) {
+  int32_t* counter = a.counters + static_cast<int64_t>(b) * a.kv_heads + g;
+  if (tid == 0) last = atomicAdd(counter, 1) == static_cast<int32_t>(gridDim.x) - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int used = static_cast<int>((len + C - 1) / C);
+  const float* pb = a.part + (static_cast<int64_t>(b) * a.heads + h0) * head_part;
+  for (int task = tid; task < G * kDecD; task += kDecThreads) {
+    const int hh = task / kDecD, d = task % kDecD;
+    const float* ph = pb + hh * head_part;
     float mx = -INFINITY;
-    for (int j = lane; j < cnt; j += 32) mx = fmaxf(mx, p_s[hh * a.chunk + j]);
-    mx = WarpMax(mx);
-    float sum = 0.f;
-    for (int j = lane; j < cnt; j += 32) {
-      const float p = expf(p_s[hh * a.chunk + j] - mx);
-      p_s[hh * a.chunk + j] = p;
-      sum += p;
+    for (int cc = 0; cc < used; ++cc) mx = fmaxf(mx, __ldcg(ph + cc * kPart + kDecD));
+    float l = 0.f, o = 0.f;
+    for (int cc = 0; cc < used; ++cc) {
+      const float w = expf(__ldcg(ph + cc * kPart + kDecD) - mx);
+      l = fmaf(__ldcg(ph + cc * kPart + kDecD + 1), w, l);
+      o = fmaf(__ldcg(ph + cc * kPart + d), w, o);
     }
-    sum = WarpSum(sum);
-    if (lane == 0) {
-      stat[2 * hh] = mx;
-      stat[2 * hh + 1] = sum;
-    }
+    a.out[static_cast<int64_t>(b) * a.out_row_stride + static_cast<int64_t>(h0 + hh) * kDecD + d] = o / l;
   }
-  __syncthreads();
-  // Weighted values: warp w takes rows w, w + 4, ...; lane owns d = 2 lane, 2 lane + 1.
-  float acc[G][2];
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = 0.f;
-  for (int j = warp; j < cnt; j += kDecThreads / 32) {
-    const float2 vv = __ldg(reinterpret_cast<const float2*>(vb + j * a.kv_row_stride) + lane);
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      const float p = p_s[hh * a.chunk + j];
-      acc[hh][0] = fmaf(p, vv.x, acc[hh][0]);
-      acc[hh][1] = fmaf(p, vv.y, acc[hh][1]);
-    }
-  }
-#pragma unroll
-  for (int hh = 0; hh < G; ++hh) {
-    red[(warp * G + hh) * kDecD + 2 * lane] = acc[hh][0];
-    red[(warp * G + hh) * kDecD + 2 * lane + 1] = acc[hh][1];
-  }
-  __syncthreads();
-  for (int i = tid; i < G * kDecD; i += blockDim.x) {
-    const int hh = i / kDecD, d = i % kDecD;
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kDecThreads / 32; ++w) s += red[(w * G + hh) * kDecD + d];
-    part_base[hh * part_head_stride + d] = s;
-  }
-  if (tid < G) {
-    part_base[tid * part_head_stride + kDecD] = stat[2 * tid];
-    part_base[tid * part_head_stride + kDecD + 1] = stat[2 * tid + 1];
-  }
-}
-
-// One warp per (sequence, head): merge the chunk partials.
-__global__ void AttnCombineKernel(const float* __restrict__ part, const int32_t* __restrict__ lens, int32_t heads,
-                                  int32_t chunk, int32_t n_chunks, float* __restrict__ out, int64_t out_row_stride,
-                                  int32_t batch) {
-  const int lane = threadIdx.x & 31;
-  const int64_t pair = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (pair >= static_cast<int64_t>(batch) * heads) return;
-  const int64_t b = pair / heads;
-  const int h = static_cast<int>(pair % heads);
-  const int used = static_cast<int>((static_cast<int64_t>(lens[b]) + chunk - 1) / chunk);
-  const float* p = part + pair * n_chunks * (kDecD + 2);
-  float mx = -INFINITY;
-  for (int c = 0; c < used; ++c) mx = fmaxf(mx, p[c * (kDecD + 2) + kDecD]);
-  float l = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int c = 0; c < used; ++c) {
-    const float* pc = p + c * (kDecD + 2);
-    const float w = expf(pc[kDecD] - mx);
-    l = fmaf(pc[kDecD + 1], w, l);
-    o0 = fmaf(pc[2 * lane], w, o0);
-    o1 = fmaf(pc[2 * lane + 1], w, o1);
-  }
-  float* orow = out + b * out_row_stride + static_cast<int64_t>(h) * kDecD;
-  orow[2 * lane] = o0 / l;
-  orow[2 * lane + 1] = o1 / l;
+  if (tid == 0) *counter = 0;
 }
 
 int LaunchRows(const RowsArgs& a, int64_t rows, cudaStream_t stream) {
@@ -289,9 +321,28 @@ int LaunchRows(const RowsArgs& a, int64_t rows, cudaStream_t stream) {
 
 template <int G>
 int LaunchDecode(const DecodeArgs& a, int32_t batch, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(G * kDecD + G * a.chunk + (kDecThreads / 32) * G * kDecD) * sizeof(float);
+  const size_t smem = static_cast<size_t>(2 * a.chunk * kDecD + G * kDecD + G * a.chunk) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaFuncSetAttribute(AttnDecodeKernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  }
   AttnDecodeKernel<G><<<dim3(a.n_chunks, a.kv_heads, batch), kDecThreads, smem, stream>>>(a);
   return CheckLaunch("attention_decode");
+}
+
+// Posts an expected byte count that no copy will ever deliver, so the
+// bounded wait runs out: the status word must then carry the timeout bit and
+// the context must stay usable. Used by the failure-detection test.
+__global__ void WaitSelftestKernel(int32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    MbarInit(&bar, 1);
+    FenceBarrierInit();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) MbarArriveExpectTx(&bar, 16);
+  __syncthreads();
+  const bool ok = MbarWait(&bar, 0);
+  if (!ok && threadIdx.x == 0) atomicOr(status, ACCEL_B200_STATUS_COPY_TIMEOUT);
 }
 
 }  // namespace
@@ -317,6 +368,7 @@ ACCEL_B200_API int accel_b200_attention(const float* q, const float* k, const fl
   a.k = k;
   a.v = v;
   a.kv_row_stride = kv_heads * head_dim;
+  a.kv_head_stride = head_dim;
   a.kv_seq_stride = 0;
   a.out = out;
   a.out_row_stride = heads * head_dim;
@@ -329,7 +381,8 @@ ACCEL_B200_API int accel_b200_attention(const float* q, const float* k, const fl
 }
 
 ACCEL_B200_API int accel_b200_attention_rows(const float* q, int64_t q_row_stride, const float* k, const float* v,
-                                             int64_t kv_row_stride, int64_t kv_seq_stride, float* out,
+                                             int64_t kv_row_stride, int64_t kv_head_stride, int64_t kv_seq_stride,
+                                             float* out,
                                              int64_t out_row_stride, const int32_t* row_seq, const int32_t* row_pos,
                                              int64_t rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
                                              void* stream) {
@@ -338,35 +391,37 @@ ACCEL_B200_API int accel_b200_attention_rows(const float* q, int64_t q_row_strid
     return SetError(ACCEL_B200_EINVAL, "attention_rows: bad arguments");
   }
   if (rows == 0) return ClearError();
-  RowsArgs a{q, q_row_stride, k, v, kv_row_stride, kv_seq_stride, out, out_row_stride, row_seq, row_pos, 0,
+  RowsArgs a{q, q_row_stride, k, v, kv_row_stride, kv_head_stride, kv_seq_stride, out, out_row_stride, row_seq, row_pos, 0,
              heads, kv_heads, head_dim, 1.f / sqrtf(static_cast<float>(head_dim))};
   return LaunchRows(a, rows, AsStream(stream));
 }
 
-ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32_t heads, int32_t max_len,
-                                                            int32_t chunk) {
-  if (batch <= 0 || heads <= 0 || max_len <= 0 || chunk <= 0) return 0;
+ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32_t heads, int32_t kv_heads,
+                                                            int32_t max_len, int32_t chunk) {
+  if (batch <= 0 || heads <= 0 || kv_heads <= 0 || max_len <= 0 || chunk <= 0) return 0;
   const int64_t chunks = (max_len + chunk - 1) / chunk;
-  return static_cast<size_t>(batch) * heads * chunks * (kDecD + 2) * sizeof(float);
+  const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int32_t) + 255) / 256 * 256;
+  return counters + static_cast<size_t>(batch) * heads * chunks * kPart * sizeof(float);
 }
 
 ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_stride, const float* k, const float* v,
-                                               int64_t kv_row_stride, int64_t kv_seq_stride, const int32_t* lens,
-                                               int32_t batch, int32_t heads, int32_t kv_heads, int32_t head_dim,
-                                               int32_t max_len, int32_t chunk, float* out, int64_t out_row_stride,
-                                               void* workspace, size_t workspace_bytes, void* stream) {
+                                               int64_t kv_row_stride, int64_t kv_head_stride, int64_t kv_seq_stride,
+                                               const int32_t* lens, int32_t batch, int32_t heads, int32_t kv_heads,
+                                               int32_t head_dim, int32_t max_len, int32_t chunk, float* out,
+                                               int64_t out_row_stride, void* workspace, size_t workspace_bytes,
+                                               int32_t* status, void* stream) {
   if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim != kDecD || max_len <= 0 ||
-      chunk <= 0 || chunk > 1024 || lens == nullptr) {
+      chunk <= 0 || chunk > 128 || lens == nullptr || q == nullptr || k == nullptr || v == nullptr || out == nullptr) {
     return SetError(ACCEL_B200_EINVAL, "attention_decode: bad arguments");
   }
   if (batch == 0) return ClearError();
   const int group = heads / kv_heads;
   if (group > kMaxGroup) return SetError(ACCEL_B200_EINVAL, "attention_decode: more than 8 query heads per kv head");
   if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16 != 0 || kv_row_stride % 4 != 0 ||
-      kv_seq_stride % 4 != 0) {
+      kv_head_stride % 4 != 0 || kv_seq_stride % 4 != 0) {
     return SetError(ACCEL_B200_EINVAL, "attention_decode: cache rows must be 16-byte aligned");
   }
-  const size_t need = accel_b200_attention_decode_workspace(batch, heads, max_len, chunk);
+  const size_t need = accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk);
   if (workspace == nullptr || workspace_bytes < need) return SetError(ACCEL_B200_EINVAL, "attention_decode: workspace too small");
   DecodeArgs a{};
   a.q = q;
@@ -374,6 +429,7 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
   a.k = k;
   a.v = v;
   a.kv_row_stride = kv_row_stride;
+  a.kv_head_stride = kv_head_stride;
   a.kv_seq_stride = kv_seq_stride;
   a.lens = lens;
   a.heads = heads;
@@ -381,24 +437,29 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
   a.chunk = chunk;
   a.n_chunks = (max_len + chunk - 1) / chunk;
   a.scale = 1.f / sqrtf(static_cast<float>(head_dim));
-  a.part = static_cast<float*>(workspace);
+  const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int32_t) + 255) / 256 * 256;
+  a.counters = static_cast<int32_t*>(workspace);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.status = status;
+  a.out = out;
+  a.out_row_stride = out_row_stride;
   cudaStream_t s = AsStream(stream);
-  int rc;
   switch (group) {
-    case 1: rc = LaunchDecode<1>(a, batch, s); break;
-    case 2: rc = LaunchDecode<2>(a, batch, s); break;
-    case 3: rc = LaunchDecode<3>(a, batch, s); break;
-    case 4: rc = LaunchDecode<4>(a, batch, s); break;
-    case 5: rc = LaunchDecode<5>(a, batch, s); break;
-    case 6: rc = LaunchDecode<6>(a, batch, s); break;
-    case 7: rc = LaunchDecode<7>(a, batch, s); break;
-    default: rc = LaunchDecode<8>(a, batch, s); break;
+    case 1: return LaunchDecode<1>(a, batch, s);
+    case 2: return LaunchDecode<2>(a, batch, s);
+    case 3: return LaunchDecode<3>(a, batch, s);
+    case 4: return LaunchDecode<4>(a, batch, s);
+    case 5: return LaunchDecode<5>(a, batch, s);
+    case 6: return LaunchDecode<6>(a, batch, s);
+    case 7: return LaunchDecode<7>(a, batch, s);
+    default: return LaunchDecode<8>(a, batch, s);
   }
-  if (rc != ACCEL_B200_OK) return rc;
-  const int64_t pairs = static_cast<int64_t>(batch) * heads;
-  AttnCombineKernel<<<static_cast<unsigned>(CeilDiv(pairs, 4)), 128, 0, s>>>(a.part, lens, heads, chunk, a.n_chunks, out,
-                                                                             out_row_stride, batch);
-  return CheckLaunch("attention_combine");
+}
+
+ACCEL_B200_API int accel_b200_wait_selftest(int32_t* status, void* stream) {
+  if (status == nullptr) return SetError(ACCEL_B200_EINVAL, "wait_selftest: null status");
+  WaitSelftestKernel<<<1, 32, 0, AsStream(stream)>>>(status);
+  return CheckLaunch("wait_selftest");
 }
 
 }  // extern "C"

@@ -34,7 +34,8 @@ __device__ __forceinline__ void RotatePair(float a, float b, const float* c, con
 __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ row_seq,
                                  const int32_t* __restrict__ row_pos, int32_t heads, int32_t kv_heads,
                                  int32_t head_dim, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                 float* __restrict__ k_cache, float* __restrict__ v_cache, int64_t seq_stride) {
+                                 float* __restrict__ k_cache, float* __restrict__ v_cache, int64_t seq_stride,
+                                 int64_t head_stride, int64_t row_stride) {
   const int64_t r = blockIdx.x;
   const int64_t pos = row_pos[r];
   if (pos < 0) return;
@@ -44,8 +45,8 @@ __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int3
   const float* s = sin_t + pos * head_dim;
   float* row = qkv + r * ld;
   const int64_t kvd = static_cast<int64_t>(kv_heads) * head_dim;
-  float* krow = k_cache + seq * seq_stride + pos * kvd;
-  float* vrow = v_cache + seq * seq_stride + pos * kvd;
+  float* kslot = k_cache + seq * seq_stride + pos * row_stride;
+  float* vslot = v_cache + seq * seq_stride + pos * row_stride;
   const int q_pairs = heads * half, k_pairs = kv_heads * half;
   for (int p = threadIdx.x; p < q_pairs; p += blockDim.x) {
     const int h = p / half, i = p % half;
@@ -61,11 +62,11 @@ __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int3
     const float* x = kin + h * head_dim;
     float lo, hi;
     RotatePair(x[i], x[half + i], c, s, i, half, &lo, &hi);
-    krow[h * head_dim + i] = lo;
-    krow[h * head_dim + half + i] = hi;
+    kslot[h * head_stride + i] = lo;
+    kslot[h * head_stride + half + i] = hi;
   }
   const float* vin = kin + kvd;
-  for (int64_t i = threadIdx.x; i < kvd; i += blockDim.x) vrow[i] = vin[i];
+  for (int64_t i = threadIdx.x; i < kvd; i += blockDim.x) vslot[(i / head_dim) * head_stride + i % head_dim] = vin[i];
 }
 
 __global__ void SiluMulRowsKernel(const float* __restrict__ gu, int64_t ld, float* __restrict__ out, int64_t ldo,
@@ -192,7 +193,8 @@ extern "C" {
 ACCEL_B200_API int accel_b200_rope_append(float* qkv, int64_t qkv_ld, const int32_t* row_seq, const int32_t* row_pos,
                                           int64_t rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
                                           const float* cos_table, const float* sin_table, float* k_cache,
-                                          float* v_cache, int64_t cache_seq_stride, void* stream) {
+                                          float* v_cache, int64_t cache_seq_stride, int64_t cache_head_stride,
+                                          int64_t cache_row_stride, void* stream) {
   if (rows < 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0 || row_pos == nullptr ||
       qkv_ld < static_cast<int64_t>(heads + 2 * kv_heads) * head_dim) {
     return SetError(ACCEL_B200_EINVAL, "rope_append: bad arguments");
@@ -201,7 +203,7 @@ ACCEL_B200_API int accel_b200_rope_append(float* qkv, int64_t qkv_ld, const int3
   if (rows > 2147483647LL) return SetError(ACCEL_B200_EINVAL, "rope_append: too many rows");
   RopeAppendKernel<<<static_cast<unsigned>(rows), 128, 0, AsStream(stream)>>>(
       qkv, qkv_ld, row_seq, row_pos, heads, kv_heads, head_dim, cos_table, sin_table, k_cache, v_cache,
-      cache_seq_stride);
+      cache_seq_stride, cache_head_stride, cache_row_stride);
   return CheckLaunch("rope_append");
 }
 

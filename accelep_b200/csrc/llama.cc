@@ -406,8 +406,13 @@ class Engine {
     std::vector<int32_t> cnt(static_cast<size_t>(batch));
     fin.Ensure(static_cast<size_t>(batch) * 4 + 16);
     Cuda(cudaMemcpyAsync(fin.p, count.p, batch * 4, cudaMemcpyDeviceToHost, stream), "counts");
+    Cuda(cudaMemcpyAsync(fin.as<int32_t>() + batch, status.p, 4, cudaMemcpyDeviceToHost, stream), "status");
     Cuda(cudaStreamSynchronize(stream), "counts");
     std::memcpy(cnt.data(), fin.p, cnt.size() * 4);
+    if (fin.as<int32_t>()[batch] != 0) {
+      Cuda(cudaMemsetAsync(status.p, 0, 4, stream), "status");
+      throw std::runtime_error("a decode attention copy did not complete within its wait bound");
+    }
     if (single) {
       Cuda(cudaMemcpy(out_ids, ids.p, static_cast<size_t>(cnt[0]) * 4, cudaMemcpyDeviceToHost), "ids");
       NoteBytesToHost(static_cast<size_t>(cnt[0]) * 4);
@@ -449,9 +454,15 @@ class Engine {
         nrows > cfg.context || out == nullptr) {
       throw std::invalid_argument("invalid cache read");
     }
+    // Head-major in HBM; the reference layout [rows, kv_heads, head_dim] on the host.
     const DevBuf& c = which == 0 ? k_cache[static_cast<size_t>(layer)] : v_cache[static_cast<size_t>(layer)];
-    const float* src = c.as<float>() + static_cast<int64_t>(slot) * cfg.context * kv_out;
-    Cuda(cudaMemcpyAsync(out, src, static_cast<size_t>(nrows) * kv_out * 4, cudaMemcpyDeviceToHost, stream), "cache");
+    const int64_t head_stride = static_cast<int64_t>(cfg.context) * head_dim;
+    const float* src = c.as<float>() + static_cast<int64_t>(slot) * head_stride * cfg.kv_heads;
+    for (int32_t g = 0; g < cfg.kv_heads && nrows > 0; ++g) {
+      Cuda(cudaMemcpy2DAsync(out + g * head_dim, kv_out * 4, src + g * head_stride, head_dim * 4, head_dim * 4, nrows,
+                             cudaMemcpyDeviceToHost, stream),
+           "cache");
+    }
     Cuda(cudaStreamSynchronize(stream), "cache");
   }
 
@@ -558,7 +569,9 @@ class Engine {
       ws = std::max(ws, GemmWorkspace(lm_head, std::min<int64_t>(m, seqs)));
     }
     moved |= gemm_ws.Ensure(ws);
-    moved |= attn_ws.Ensure(accel_b200_attention_decode_workspace(seqs, cfg.heads, cfg.context, kDecodeChunk));
+    moved |= attn_ws.Ensure(
+        accel_b200_attention_decode_workspace(seqs, cfg.heads, cfg.kv_heads, cfg.context, kDecodeChunk));
+    moved |= status.Ensure(16);
     if (moved) DropGraphs();
   }
 
@@ -591,7 +604,11 @@ class Engine {
   void Forward(int64_t rows, int32_t seqs, bool decode) {
     const int64_t H = cfg.hidden, I = cfg.intermediate;
     const int64_t qkv_ld = q_out + 2 * kv_out;
-    const int64_t slot_stride = static_cast<int64_t>(cfg.context) * kv_out;
+    // Head-major cache: slot -> kv head -> row -> dim, so one (sequence, kv
+    // head) chunk of rows is one contiguous block for the decode kernel.
+    const int64_t row_stride = head_dim;
+    const int64_t head_stride = static_cast<int64_t>(cfg.context) * head_dim;
+    const int64_t slot_stride = head_stride * cfg.kv_heads;
     const int32_t* tok = decode ? pre_tokens() : tokens.as<int32_t>();
     const int32_t* rseq = decode ? dec_seq.as<int32_t>() : row_seq.as<int32_t>();
     const int32_t* rpos = decode ? dec_pos.as<int32_t>() : row_pos.as<int32_t>();
@@ -608,15 +625,17 @@ class Engine {
       Abi(accel_b200_rmsnorm(hid, l.attn_norm.as<float>(), normed.as<float>(), rows, H, cfg.eps, 0, stream));
       Gemm(normed.as<float>(), H, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr);
       Abi(accel_b200_rope_append(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
-                                 rope_cos.as<float>(), rope_sin.as<float>(), kc, vc, slot_stride, stream));
+                                 rope_cos.as<float>(), rope_sin.as<float>(), kc, vc, slot_stride, head_stride,
+                                 row_stride, stream));
       if (decode && head_dim == 64) {
-        Abi(accel_b200_attention_decode(qkv.as<float>(), qkv_ld, kc, vc, kv_out, slot_stride, lens.as<int32_t>(), seqs,
-                                        cfg.heads, cfg.kv_heads, head_dim, cfg.context, kDecodeChunk, mixed.as<float>(),
-                                        q_out, attn_ws.p, attn_ws.bytes, stream));
+        Abi(accel_b200_attention_decode(qkv.as<float>(), qkv_ld, kc, vc, row_stride, head_stride, slot_stride,
+                                        lens.as<int32_t>(), seqs, cfg.heads, cfg.kv_heads, head_dim, cfg.context,
+                                        kDecodeChunk, mixed.as<float>(), q_out, attn_ws.p, attn_ws.bytes,
+                                        status.as<int32_t>(), stream));
       } else {
-        Abi(accel_b200_attention_rows(qkv.as<float>(), qkv_ld, kc, vc, kv_out, slot_stride, mixed.as<float>(), q_out,
-                                      rseq, decode ? dec_len_pos() : rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
-                                      stream));
+        Abi(accel_b200_attention_rows(qkv.as<float>(), qkv_ld, kc, vc, row_stride, head_stride, slot_stride,
+                                      mixed.as<float>(), q_out, rseq, decode ? dec_len_pos() : rpos, rows, cfg.heads,
+                                      cfg.kv_heads, head_dim, stream));
       }
       Gemm(mixed.as<float>(), q_out, l.o, rows, hid, H, &residual);
       Abi(accel_b200_rmsnorm(hid, l.post_norm.as<float>(), normed.as<float>(), rows, H, cfg.eps, 0, stream));
@@ -681,7 +700,7 @@ class Engine {
     }
   }
 
-  static constexpr int32_t kDecodeChunk = 256;
+  static constexpr int32_t kDecodeChunk = 64;
 
   DevBuf embed, final_norm, rope_cos, rope_sin;
   std::vector<Layer> layers;
@@ -693,7 +712,7 @@ class Engine {
   DevBuf ids;
   int32_t ids_rows = 0;
   int64_t ids_stride = 0;
-  DevBuf gemm_ws, attn_ws;
+  DevBuf gemm_ws, attn_ws, status;
   PinnedBuf staging, finished_host;
   cudaGraphExec_t graph_exec = nullptr;
   std::tuple<int32_t, bool, float, int32_t, int32_t> graph_key;

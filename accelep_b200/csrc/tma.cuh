@@ -1,0 +1,73 @@
+// Bulk-copy (TMA) and mbarrier helpers in inline PTX for sm_100a.
+//
+// Only the untiled global -> shared bulk copy is used here, with a CTA-local
+// destination and no cluster multicast: every copy reads this GPU's own
+// memory into this CTA's shared memory. Waits on an mbarrier are bounded;
+// a wait that runs out reports failure to its caller instead of spinning on.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace accel_b200 {
+
+// Upper bound on the wait for one mbarrier phase: one second of the global
+// timer, far beyond any real copy latency (microseconds).
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint64_t GlobalTimerNs() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t SmemAddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void MbarInit(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(SmemAddr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void FenceBarrierInit() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One arrival that also announces `bytes` of incoming transactions.
+__device__ __forceinline__ void MbarArriveExpectTx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(SmemAddr(bar)), "r"(bytes) : "memory");
+}
+
+// Global -> shared bulk copy completing on `bar`. dst, src and bytes must be
+// multiples of 16.
+__device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(SmemAddr(dst)),
+      "l"(src), "r"(bytes), "r"(SmemAddr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(SmemAddr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete; false when the bound ran out.
+__device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = GlobalTimerNs();
+  for (;;) {
+    for (int i = 0; i < 64; ++i) {
+      if (MbarTryWait(bar, parity)) return true;
+    }
+    if (GlobalTimerNs() - start > kWaitLimitNs) return false;
+  }
+}
+
+}  // namespace accel_b200

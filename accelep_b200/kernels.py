@@ -113,6 +113,8 @@ def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none
     ep.act = ACT[act]
     ep.residual = 0 if residual is None else residual.data_ptr()
     ep.residual_ld = 0 if residual is None else residual.stride(0)
+    # The struct holds raw addresses: keep the tensors alive with it.
+    ep._keep = (bias, residual)
     return ep
 
 
@@ -167,15 +169,26 @@ def matmul_f32(a, b, epilogue=None, out=None):
     return c
 
 
-def attention_decode(q, k_cache, v_cache, lens, heads, kv_heads, head_dim, max_len, chunk=256):
-    """q [B, heads * head_dim]; caches [B, max_len, kv_heads, head_dim]."""
+def attention_decode(q, k_cache, v_cache, lens, heads, kv_heads, head_dim, max_len, chunk=64, head_major=False,
+                     workspace=None, status=None):
+    """q [B, heads * head_dim]. Caches [B, max_len, kv_heads, head_dim] (the
+    reference layout) or, with head_major, [B, kv_heads, max_len, head_dim]."""
     lib = load()
     batch = q.shape[0]
     out = torch.zeros(batch, heads * head_dim, dtype=torch.float32, device=q.device)
-    need = lib.accel_b200_attention_decode_workspace(batch, heads, max_len, chunk)
-    ws = _workspace(q.device, need)
-    kvd = kv_heads * head_dim
-    check(lib.accel_b200_attention_decode(_p(q), q.stride(0), _p(k_cache), _p(v_cache), kvd, max_len * kvd, _p(lens),
-                                          batch, heads, kv_heads, head_dim, max_len, chunk, _p(out), out.stride(0),
-                                          _p(ws), ws.numel(), _s()))
+    need = lib.accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk)
+    ws = workspace if workspace is not None else torch.zeros(need, dtype=torch.uint8, device=q.device)
+    if head_major:
+        row, head, seq = head_dim, max_len * head_dim, kv_heads * max_len * head_dim
+    else:
+        row, head, seq = kv_heads * head_dim, head_dim, max_len * kv_heads * head_dim
+    check(lib.accel_b200_attention_decode(_p(q), q.stride(0), _p(k_cache), _p(v_cache), row, head, seq, _p(lens), batch,
+                                          heads, kv_heads, head_dim, max_len, chunk, _p(out), out.stride(0), _p(ws),
+                                          ws.numel(), _p(status), _s()))
     return out
+
+
+def attention_decode_workspace(batch, heads, kv_heads, max_len, chunk=64, device="cuda"):
+    """A zeroed workspace for attention_decode (its counters start at zero)."""
+    need = load().accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk)
+    return torch.zeros(need, dtype=torch.uint8, device=device)

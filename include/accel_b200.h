@@ -44,8 +44,9 @@ enum {
 /* Activation codes: include/accel/device.h:11 (Activation::None/Relu/Gelu). */
 enum { ACCEL_B200_ACT_NONE = 0, ACCEL_B200_ACT_RELU = 1, ACCEL_B200_ACT_GELU = 2 };
 
-/* Bits of a device status word written by kernels that validate data. */
-enum { ACCEL_B200_STATUS_BAD_TOKEN = 1 };
+/* Bits of a device status word written by kernels that validate data or
+   that gave up a bounded wait. */
+enum { ACCEL_B200_STATUS_BAD_TOKEN = 1, ACCEL_B200_STATUS_COPY_TIMEOUT = 2 };
 
 ACCEL_B200_API const char* accel_b200_last_error(void);
 /* Number of kernel launches this library has issued in this process
@@ -184,33 +185,45 @@ ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const floa
    (src/llama_model.cc:229-232) over fused projection rows
    qkv[r] = [q (heads * head_dim) | k (kv_heads * head_dim) | v]. Queries are
    rotated in place; keys and values land in cache row row_pos[r] of slot
-   row_seq[r] (row_seq may be NULL: slot 0). A cache slot is [context,
-   kv_heads, head_dim]; slots are cache_seq_stride floats apart. Bit-exact. */
+   row_seq[r] (row_seq may be NULL: slot 0). Element (slot s, kv head g,
+   row t, dim d) of a cache is at s * seq_stride + g * head_stride + t *
+   row_stride + d (floats): the reference layout [context, kv_heads,
+   head_dim] is (head_stride, row_stride) = (head_dim, kv_heads * head_dim).
+   Bit-exact. */
 ACCEL_B200_API int accel_b200_rope_append(float* qkv, int64_t qkv_ld, const int32_t* row_seq, const int32_t* row_pos,
                                           int64_t rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
                                           const float* cos_table, const float* sin_table, float* k_cache,
-                                          float* v_cache, int64_t cache_seq_stride, void* stream);
+                                          float* v_cache, int64_t cache_seq_stride, int64_t cache_head_stride,
+                                          int64_t cache_row_stride, void* stream);
 
 /* Causal attention of each row over its own sequence's cache rows
    [0, row_pos[r]] (src/sim_attend.cc:9-46 with per-row sequence and
-   position). q row r: q + r * q_row_stride; cache row t of slot s: k + s *
-   kv_seq_stride + t * kv_row_stride. */
+   position). q row r: q + r * q_row_stride; cache strides as in
+   accel_b200_rope_append. */
 ACCEL_B200_API int accel_b200_attention_rows(const float* q, int64_t q_row_stride, const float* k, const float* v,
-                                             int64_t kv_row_stride, int64_t kv_seq_stride, float* out,
-                                             int64_t out_row_stride, const int32_t* row_seq, const int32_t* row_pos,
-                                             int64_t rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
-                                             void* stream);
+                                             int64_t kv_row_stride, int64_t kv_head_stride, int64_t kv_seq_stride,
+                                             float* out, int64_t out_row_stride, const int32_t* row_seq,
+                                             const int32_t* row_pos, int64_t rows, int32_t heads, int32_t kv_heads,
+                                             int32_t head_dim, void* stream);
 
 /* Split-KV decode attention, head_dim 64: one query row per sequence b over
-   cache rows [0, lens[b]) of slot b (1 <= lens[b] <= max_len). Context chunks
-   of `chunk` rows are reduced in parallel into `workspace` and merged. */
-ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32_t heads, int32_t max_len,
-                                                            int32_t chunk);
+   cache rows [0, lens[b]) of slot b (1 <= lens[b] <= max_len; cache strides
+   as in accel_b200_rope_append, 16-byte aligned). Chunks of `chunk` (<= 128)
+   rows are reduced in parallel into `workspace` and merged in chunk order by
+   the last CTA of each (sequence, kv head). The workspace must hold
+   accel_b200_attention_decode_workspace(...) bytes whose first
+   batch * kv_heads int32 arrival counters are zero before the first call;
+   every call leaves them zero. Calls that share a workspace must not overlap
+   on the GPU. A bulk copy that does not land within the wait bound ORs
+   ACCEL_B200_STATUS_COPY_TIMEOUT into *status (device int; may be NULL). */
+ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32_t heads, int32_t kv_heads,
+                                                            int32_t max_len, int32_t chunk);
 ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_stride, const float* k, const float* v,
-                                               int64_t kv_row_stride, int64_t kv_seq_stride, const int32_t* lens,
-                                               int32_t batch, int32_t heads, int32_t kv_heads, int32_t head_dim,
-                                               int32_t max_len, int32_t chunk, float* out, int64_t out_row_stride,
-                                               void* workspace, size_t workspace_bytes, void* stream);
+                                               int64_t kv_row_stride, int64_t kv_head_stride, int64_t kv_seq_stride,
+                                               const int32_t* lens, int32_t batch, int32_t heads, int32_t kv_heads,
+                                               int32_t head_dim, int32_t max_len, int32_t chunk, float* out,
+                                               int64_t out_row_stride, void* workspace, size_t workspace_bytes,
+                                               int32_t* status, void* stream);
 
 /* SiluMul (src/sim_silu.cc:8-13) over fused rows [gate (inter) | up (inter)]
    of row stride ld into out[r, i] (row stride ldo). */
@@ -236,6 +249,12 @@ ACCEL_B200_API int accel_b200_greedy_step(const float* logits, const int32_t* pr
                                           int32_t* tokens, int32_t* row_pos, int32_t* lens, int32_t eos,
                                           int32_t context, int32_t* step, int32_t* finished, int32_t batch,
                                           void* stream);
+
+/* Runs one CTA whose bulk-copy wait can never be satisfied: after the one-
+   second wait bound it ORs ACCEL_B200_STATUS_COPY_TIMEOUT into *status and
+   returns, leaving the context usable. Exercises the bounded-wait error path
+   without a fault. */
+ACCEL_B200_API int accel_b200_wait_selftest(int32_t* status, void* stream);
 
 /* dst[r, :] = src[idx[r], :] for r < rows (cols floats per row): the last
    prompt row of each sequence before the final norm (src/llama_model.cc:244). */

@@ -125,10 +125,19 @@ def test_attention_decode_split(lib, cuda, orc):
     vc = rng.standard_normal((batch, max_len, kvh, hd), dtype=np.float32)
     q = rng.standard_normal((batch, heads * hd), dtype=np.float32)
     got = H(K.attention_decode(T(q), T(kc), T(vc), T(lens, torch.int32), heads, kvh, hd, max_len))
+    # The engine's head-major layout, one row per bulk copy vs one per chunk.
+    hm = H(K.attention_decode(T(q), T(kc.transpose(0, 2, 1, 3)), T(vc.transpose(0, 2, 1, 3)), T(lens, torch.int32),
+                              heads, kvh, hd, max_len, head_major=True))
+    ws = K.attention_decode_workspace(batch, heads, kvh, max_len)
+    for _ in range(2):  # a reused workspace: the arrival counters return to zero
+        again = H(K.attention_decode(T(q), T(kc), T(vc), T(lens, torch.int32), heads, kvh, hd, max_len, workspace=ws))
+        assert np.array_equal(again, got)
+    assert not H(ws[:batch * kvh * 4]).any()
     for b in range(batch):
         n = int(lens[b])
         want = orc.attend(q[b].reshape(1, heads, hd), kc[b, :n], vc[b, :n], 1, n - 1, heads, kvh, hd)
         close(got[b], want.reshape(-1))
+        close(hm[b], want.reshape(-1))
 
 
 def test_silu_add(lib, cuda, small, kats):

@@ -36,12 +36,14 @@ def test_tiny_generate_matches_reference(tiny, small):
     assert np.array_equal(tiny.generate(p, 40, temperature=1.1, seed=9, top_k=0), small["tiny_full"])
 
 
-def test_tiny_logits_and_cache(tiny, orc):
+def test_tiny_logits_and_cache(lib, cuda, orc):
     from oracle.oracle import LlamaHandle
 
     cfg = syn.TINY_LLAMA
     ref = LlamaHandle(orc, cfg)
     ref.load(syn.llama_weights(cfg, 5))
+    tiny = Llama(cfg)  # a fresh model: its cache rows start at zero
+    tiny.load_fp32(syn.llama_weights(cfg, 5))
     p = syn.prompts(cfg, 1, 9, 21)[0]
     for ids, reset in ((p, True), (p[:1], False), (p[:4], False)):
         tiny.forward_ids(ids, reset)
@@ -58,6 +60,7 @@ def test_tiny_logits_and_cache(tiny, orc):
             np.testing.assert_allclose(got[:filled], want[:filled], rtol=TOL, atol=TOL)
             # Rows past the fill were never written: indexing is exact.
             assert not got[filled:].any()
+    tiny.close()
 
 
 def test_tiny_eos_and_full_context(tiny, orc):
