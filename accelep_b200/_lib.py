@@ -59,6 +59,7 @@ SIGNATURES = {
     "accel_b200_transpose": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp]),
     "accel_b200_gemm_epilogue": (c_int, [c_vp, c_i64, c_i64, c_f32, c_vp, P_i64, c_i32, c_f32, c_i32, c_vp]),
     "accel_b200_matmul_q8_workspace": (c_sz, [c_i64, c_i64, c_i64]),
+    "accel_b200_set_q8_path": (c_int, [c_i32]),
     "accel_b200_matmul_q8": (c_int, [c_vp, c_i64, P_plane, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_matmul_f32_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_f32": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),

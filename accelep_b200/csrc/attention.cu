@@ -400,8 +400,7 @@ ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32
                                                             int32_t max_len, int32_t chunk) {
   if (batch <= 0 || heads <= 0 || kv_heads <= 0 || max_len <= 0 || chunk <= 0) return 0;
   const int64_t chunks = (max_len + chunk - 1) / chunk;
-  const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int32_t) + 255) / 256 * 256;
-  return counters + static_cast<size_t>(batch) * heads * chunks * kPart * sizeof(float);
+  return kCounterRegion + static_cast<size_t>(batch) * heads * chunks * kPart * sizeof(float);
 }
 
 ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_stride, const float* k, const float* v,
@@ -437,9 +436,11 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
   a.chunk = chunk;
   a.n_chunks = (max_len + chunk - 1) / chunk;
   a.scale = 1.f / sqrtf(static_cast<float>(head_dim));
-  const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int32_t) + 255) / 256 * 256;
+  if (static_cast<int64_t>(batch) * kv_heads > kMaxCounters) {
+    return SetError(ACCEL_B200_EINVAL, "attention_decode: batch * kv_heads above 16384");
+  }
   a.counters = static_cast<int32_t*>(workspace);
-  a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegion);
   a.status = status;
   a.out = out;
   a.out_row_stride = out_row_stride;

@@ -21,6 +21,12 @@ inline cudaStream_t AsStream(void* s) { return static_cast<cudaStream_t>(s); }
 
 inline int64_t CeilDiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Product workspaces start with a fixed region of arrival counters that the
+// kernels leave zero; split-K partial sums follow it. The fixed offset keeps
+// the counters of every call on the same zeroed bytes whatever the shape.
+constexpr size_t kCounterRegion = 64 * 1024;
+constexpr int64_t kMaxCounters = static_cast<int64_t>(kCounterRegion / sizeof(int32_t));
+
 __host__ __device__ __forceinline__ int64_t Min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t Max64(int64_t a, int64_t b) { return a > b ? a : b; }
 

@@ -380,6 +380,7 @@ class B200Device final : public accel::Device {
         workspace_ = nullptr;
       }
       CheckCuda(cudaMalloc(&workspace_, bytes), "workspace");
+      CheckCuda(cudaMemsetAsync(workspace_, 0, bytes, stream_), "workspace");  // arrival counters start at zero
       workspace_bytes_ = bytes;
     }
     return workspace_;

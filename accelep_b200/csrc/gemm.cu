@@ -18,6 +18,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "accel_b200.h"
 #include "common.cuh"
 
@@ -274,9 +276,9 @@ int RunGemm(GemmArgs g, cudaStream_t s, void* workspace, size_t workspace_bytes)
   if (p.row_blocks > 65535 || p.splits > 65535) return SetError(ACCEL_B200_EINVAL, "matmul: grid too large");
   g.k_per_split = p.k_per_split;
   if (p.splits > 1) {
-    const size_t need = static_cast<size_t>(p.splits) * g.m * g.n * sizeof(float);
+    const size_t need = kCounterRegion + static_cast<size_t>(p.splits) * g.m * g.n * sizeof(float);
     if (workspace == nullptr || workspace_bytes < need) return SetError(ACCEL_B200_EINVAL, "matmul: workspace too small");
-    g.part = static_cast<float*>(workspace);
+    g.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegion);
   }
   switch (p.mt * 100 + p.vec) {
     case 116: LaunchKn<W, 1, 16>(g, p, s); break;
@@ -300,7 +302,7 @@ int RunGemm(GemmArgs g, cudaStream_t s, void* workspace, size_t workspace_bytes)
 size_t WorkspaceFor(bool int8, int64_t m, int64_t k, int64_t n) {
   if (m <= 0 || k <= 0 || n <= 0) return 0;
   const Plan p = MakePlan(int8, m, k, n);
-  return p.splits > 1 ? static_cast<size_t>(p.splits) * m * n * sizeof(float) : 0;
+  return p.splits > 1 ? kCounterRegion + static_cast<size_t>(p.splits) * m * n * sizeof(float) : 0;
 }
 
 bool ToEpilogue(const accel_b200_epilogue* in, Epilogue* out) {
@@ -334,6 +336,25 @@ int EmptySum(float* c, int64_t ldc, int64_t m, int64_t n, const Epilogue& ep, cu
 }
 
 }  // namespace
+
+// Tensor-core path (gemm_tc.cu).
+bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
+                int64_t n);
+size_t TcWorkspace(int64_t m, int64_t k, int64_t n);
+int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c, int64_t ldc,
+          int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace, size_t workspace_bytes,
+          int32_t* status, cudaStream_t stream);
+
+namespace {
+std::atomic<int> g_q8_path{0};  // 0: by shape, 1: CUDA cores, 2: tensor cores where eligible
+
+bool UseTc(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
+           int64_t n) {
+  const int path = g_q8_path.load(std::memory_order_relaxed);
+  if (path == 1) return false;
+  return TcEligible(a, lda, w, axis, zero, m, k, n);
+}
+}  // namespace
 }  // namespace accel_b200
 
 using namespace accel_b200;
@@ -351,7 +372,16 @@ ACCEL_B200_API int accel_b200_matmul(const float* a, const float* b, float* c, i
 }
 
 ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64_t n) {
-  return WorkspaceFor(true, m, k, n);
+  // Enough for either path, so the caller need not know which one runs.
+  const size_t simt = WorkspaceFor(true, m, k, n);
+  const size_t tc = (m > 0 && k > 0 && n > 0) ? TcWorkspace(m, k, n) : 0;
+  return simt > tc ? simt : tc;
+}
+
+ACCEL_B200_API int accel_b200_set_q8_path(int32_t path) {
+  if (path < 0 || path > 2) return SetError(ACCEL_B200_EINVAL, "set_q8_path: 0 (by shape), 1 (CUDA cores) or 2");
+  g_q8_path.store(path, std::memory_order_relaxed);
+  return ClearError();
 }
 
 ACCEL_B200_API size_t accel_b200_matmul_f32_workspace(int64_t m, int64_t k, int64_t n) {
@@ -372,9 +402,14 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
   if (a == nullptr || lda < k || b->q == nullptr || b->scale == nullptr) {
     return SetError(ACCEL_B200_EINVAL, "quantized MatMul is missing an operand");
   }
+  const int8_t* w = b->q + b->offset;
+  if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
+    return RunTc(a, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace, workspace_bytes, nullptr,
+                 AsStream(stream));
+  }
   g.a = a;
   g.lda = lda;
-  g.w = b->q + b->offset;
+  g.w = w;
   g.scale = b->scale;
   g.zero = b->zero;
   g.axis = b->axis;

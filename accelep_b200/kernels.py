@@ -119,7 +119,8 @@ def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none
 
 
 class Workspace:
-    """Grows a device byte buffer on demand."""
+    """Grows a zero-filled device byte buffer on demand (the kernels keep
+    arrival counters in it and leave them zero)."""
 
     def __init__(self, device="cuda"):
         self.device = device
@@ -129,8 +130,13 @@ class Workspace:
         if nbytes == 0:
             return None
         if self.buf is None or self.buf.numel() < nbytes:
-            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         return self.buf
+
+
+def set_q8_path(path):
+    """0: by shape (tensor cores where eligible), 1: CUDA cores only."""
+    check(load().accel_b200_set_q8_path(path))
 
 
 _WS = {}

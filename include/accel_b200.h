@@ -153,16 +153,22 @@ typedef struct accel_b200_epilogue {
   int64_t residual_ld;
 } accel_b200_epilogue;
 
-/* Scratch, in bytes, accel_b200_matmul_q8 needs for these sizes (0 when the
-   product runs in one pass). */
+/* Scratch, in bytes, accel_b200_matmul_q8 needs for these sizes. */
 ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64_t n);
+
+/* Which kernel accel_b200_matmul_q8 uses, process-wide: 0 by shape (the
+   default: the tcgen05 tensor-core kernel for per-column or single scales
+   without zero points and 16-byte aligned rows, CUDA cores otherwise), 1
+   CUDA cores only, 2 the same as 0. For comparisons and tests. */
+ACCEL_B200_API int accel_b200_set_q8_path(int32_t path);
 
 /* src/sim_device.cc:541-602 (MatMulQuantized with a right-hand plane) and
    the epilogue the runtime applies after it (src/runtime.cc:326-344):
    c[m, n] = epilogue(A[m, k] @ dequant(B)), with A fp32 row-major (row
    stride lda) and C row stride ldc. ep may be NULL (plain product).
-   workspace must hold accel_b200_matmul_q8_workspace(m, k, n) bytes (it may
-   be NULL when that is 0); concurrent calls need separate workspaces. */
+   workspace must hold accel_b200_matmul_q8_workspace(m, k, n) bytes whose
+   first 64 KiB were zero before the first call (arrival counters, left zero
+   by every call); calls that share a workspace must not overlap on the GPU. */
 ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c,
                                         int64_t ldc, int64_t m, int64_t k, int64_t n,
                                         const accel_b200_epilogue* ep, void* workspace, size_t workspace_bytes,
@@ -211,9 +217,9 @@ ACCEL_B200_API int accel_b200_attention_rows(const float* q, int64_t q_row_strid
    as in accel_b200_rope_append, 16-byte aligned). Chunks of `chunk` (<= 128)
    rows are reduced in parallel into `workspace` and merged in chunk order by
    the last CTA of each (sequence, kv head). The workspace must hold
-   accel_b200_attention_decode_workspace(...) bytes whose first
-   batch * kv_heads int32 arrival counters are zero before the first call;
-   every call leaves them zero. Calls that share a workspace must not overlap
+   accel_b200_attention_decode_workspace(...) bytes whose first 64 KiB
+   (arrival counters) are zero before the first call; every call leaves them
+   zero, so one zeroed buffer serves any mix of products and attention. Calls that share a workspace must not overlap
    on the GPU. A bulk copy that does not land within the wait bound ORs
    ACCEL_B200_STATUS_COPY_TIMEOUT into *status (device int; may be NULL). */
 ACCEL_B200_API size_t accel_b200_attention_decode_workspace(int32_t batch, int32_t heads, int32_t kv_heads,

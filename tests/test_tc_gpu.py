@@ -1,0 +1,77 @@
+"""The tcgen05 int8 product (accel_b200_matmul_q8 on its tensor-core path)
+against the CPU checker and against the CUDA-core path: partial feature
+tiles, partial row tiles, K that is not a multiple of the 64-deep block,
+split K, single scales and the fused epilogue."""
+
+import numpy as np
+import pytest
+import torch
+
+from accelep_b200 import kernels as K
+from accelep_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a):
+    return torch.as_tensor(np.ascontiguousarray(a)).to("cuda")
+
+
+def H(t):
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+def check_close(got, want, k, scale_mag):
+    tol = 1e-4 + 1e-4 * np.abs(want)
+    tol = np.maximum(tol, 2 * k * np.finfo(np.float32).eps * scale_mag)
+    err = np.abs(got - want)
+    assert (err <= tol).all(), f"{(err > tol).sum()} of {err.size} outside tolerance, max err {err.max()}"
+
+
+@pytest.fixture(autouse=True)
+def by_shape():
+    K.set_q8_path(0)
+    yield
+    K.set_q8_path(0)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 64, 128), (32, 576, 960), (7, 100, 336), (33, 576, 576), (64, 1536, 576),
+                                   (100, 192, 3072), (130, 576, 1536), (300, 640, 272), (32, 1536, 49152)])
+def test_tc_matches_checker(lib, cuda, orc, m, k, n):
+    x, w, s = syn.int8_gemm(m, k, n, m + k + n)
+    res = np.random.default_rng(m).standard_normal((m, n), dtype=np.float32)
+    ep = K.make_epilogue(act="gelu", residual=T(res))
+    got = H(K.matmul_q8(T(x), T(w), T(s), epilogue=ep))
+    mag = np.abs(x).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
+    cols = slice(None) if n <= 4096 else slice(n - 300, n)
+    want = orc.execute_matmul_q(x, np.ascontiguousarray(w[:, cols]), s[cols], act="gelu",
+                                residual=np.ascontiguousarray(res[:, cols]))
+    check_close(got[:, cols], want, k, mag[:, cols])
+
+
+def test_tc_equals_cuda_core_path(lib, cuda):
+    x, w, s = syn.int8_gemm(32, 576, 960, 3)
+    xt, wt, st = T(x), T(w), T(s)
+    tc = H(K.matmul_q8(xt, wt, st))
+    K.set_q8_path(1)
+    simt = H(K.matmul_q8(xt, wt, st))
+    mag = np.abs(x).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
+    check_close(tc, simt, 576, mag)
+
+
+def test_tc_scalar_scale_and_repeat(lib, cuda, orc):
+    """axis -1 (one scale) and repeated calls on one workspace: the split-K
+    arrival counters return to zero after every call."""
+    x, w, _ = syn.int8_gemm(16, 1536, 576, 8)
+    scalar = np.array([0.004], np.float32)
+    ws = torch.zeros(K.load().accel_b200_matmul_q8_workspace(16, 1536, 576), dtype=torch.uint8, device="cuda")
+    want = orc.matmul_quantized(x, w, scalar, None, [1536, 576], -1, 0, 16, 1536, 576)
+    first = None
+    for _ in range(3):
+        got = H(K.matmul_q8(T(x), T(w), T(scalar), axis=-1, workspace=ws))
+        first = got if first is None else first
+        assert np.array_equal(got, first)  # deterministic split order
+    mag = np.abs(x).astype(np.float64) @ np.abs(w.astype(np.float64)) * 0.004
+    check_close(first, want, 1536, mag)
+    assert not H(ws[:256]).any()
