@@ -19,6 +19,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "accel_b200.h"
 #include "common.cuh"
 #include "tma.cuh"
@@ -346,6 +348,45 @@ __global__ void WaitSelftestKernel(int32_t* status) {
 }
 
 }  // namespace
+
+// ------------------------------------------- decode attention without allocation
+//
+// Scratch of accel_b200_attention_decode_noalloc: a fixed array in the
+// library's own device memory, so that callers who may not allocate still
+// have a place for the split partials and arrival counters. Every GPU that
+// loads this library holds these 4 MiB until the process exits.
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(4) << 20;
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// The device address of the scratch array on the current device. In host code
+// g_decode_scratch names a host-side stand-in, not device memory: a kernel
+// given that name would fault or read the wrong memory, so the address is
+// looked up once per device and cached.
+int ScratchAddress(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return SetError(ACCEL_B200_ECUDA, std::string("noalloc scratch: ") + cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices) return SetError(ACCEL_B200_EINVAL, "noalloc scratch: device ordinal above 63");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      return SetError(ACCEL_B200_ECUDA, std::string("noalloc scratch: cudaGetSymbolAddress failed: ") +
+                                            cudaGetErrorString(err));
+    }
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return ACCEL_B200_OK;
+}
+}  // namespace
 }  // namespace accel_b200
 
 using namespace accel_b200;
@@ -455,6 +496,39 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
     case 7: return LaunchDecode<7>(a, batch, s);
     default: return LaunchDecode<8>(a, batch, s);
   }
+}
+
+ACCEL_B200_API size_t accel_b200_attention_decode_noalloc_limit(void) { return kNoAllocScratchBytes; }
+
+ACCEL_B200_API int accel_b200_attention_decode_noalloc(const float* q, int64_t q_row_stride, const float* k,
+                                                       const float* v, int64_t kv_row_stride, int64_t kv_head_stride,
+                                                       int64_t kv_seq_stride, const int32_t* lens, int32_t batch,
+                                                       int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                                       int32_t max_len, int32_t chunk, float* out,
+                                                       int64_t out_row_stride, int32_t* status, void* stream) {
+  const size_t need = accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk);
+  if (need > kNoAllocScratchBytes) {
+    return SetError(ACCEL_B200_EINVAL,
+                    "attention_decode_noalloc: these sizes need " + std::to_string(need) +
+                        " bytes of scratch, above the fixed 4 MiB (4194304 bytes); use accel_b200_attention_decode "
+                        "with a caller-owned workspace");
+  }
+  if (batch <= 0) return accel_b200_attention_decode(q, q_row_stride, k, v, kv_row_stride, kv_head_stride,
+                                                     kv_seq_stride, lens, batch, heads, kv_heads, head_dim, max_len,
+                                                     chunk, out, out_row_stride, nullptr, 0, status, stream);
+  void* scratch = nullptr;
+  const int rc = ScratchAddress(&scratch);
+  if (rc != ACCEL_B200_OK) return rc;
+  // The array keeps whatever the last call left; the arrival counters must
+  // start at zero, so they are cleared on this call's stream first.
+  const cudaError_t err =
+      cudaMemsetAsync(scratch, 0, static_cast<size_t>(batch) * kv_heads * sizeof(int32_t), AsStream(stream));
+  if (err != cudaSuccess) {
+    return SetError(ACCEL_B200_ECUDA, std::string("attention_decode_noalloc: ") + cudaGetErrorString(err));
+  }
+  return accel_b200_attention_decode(q, q_row_stride, k, v, kv_row_stride, kv_head_stride, kv_seq_stride, lens, batch,
+                                     heads, kv_heads, head_dim, max_len, chunk, out, out_row_stride, scratch,
+                                     kNoAllocScratchBytes, status, stream);
 }
 
 ACCEL_B200_API int accel_b200_wait_selftest(int32_t* status, void* stream) {

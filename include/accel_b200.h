@@ -231,6 +231,29 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
                                                int64_t out_row_stride, void* workspace, size_t workspace_bytes,
                                                int32_t* status, void* stream);
 
+/* The same decode attention for callers that must not allocate device
+   memory: a plugin running inside a host runtime that owns all device memory
+   through its own arena (ONNX Runtime, for one), or a serving loop that forbids
+   allocation after warm-up, since cudaMalloc and cudaFree synchronize the
+   device and stall every stream. No reference counterpart: an addition of
+   this backend. The scratch is a fixed 4 MiB array in the library's own
+   device memory (accel_b200_attention_decode_noalloc_limit() bytes; each GPU
+   that loads the library holds it until the process exits); sizes whose
+   workspace would exceed it are rejected with ACCEL_B200_EINVAL. The entry
+   point calls no cudaMalloc, cudaFree or allocating library routine. The
+   first call on a device looks up the array's device address with
+   cudaGetSymbolAddress, so make that first call before any stream capture.
+   All calls share the array and each clears the arrival counters it needs on
+   its own stream; calls that overlap on the GPU (different streams, several
+   threads) race on the array. */
+ACCEL_B200_API size_t accel_b200_attention_decode_noalloc_limit(void);
+ACCEL_B200_API int accel_b200_attention_decode_noalloc(const float* q, int64_t q_row_stride, const float* k,
+                                                       const float* v, int64_t kv_row_stride, int64_t kv_head_stride,
+                                                       int64_t kv_seq_stride, const int32_t* lens, int32_t batch,
+                                                       int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                                       int32_t max_len, int32_t chunk, float* out,
+                                                       int64_t out_row_stride, int32_t* status, void* stream);
+
 /* SiluMul (src/sim_silu.cc:8-13) over fused rows [gate (inter) | up (inter)]
    of row stride ld into out[r, i] (row stride ldo). */
 ACCEL_B200_API int accel_b200_silu_mul_rows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows,
