@@ -1,30 +1,41 @@
-// int8-weight product on the 5th-generation tensor cores (tcgen05).
+// int8-weight product on the 5th-generation tensor cores (tcgen05), fed by TMA.
 //
-// C[m, n] = epilogue(scale[n] * sum_k A[m, k] * q[k, n]) with A fp32 [m, k] and q
-// int8 [k, n] (n contiguous: the reference's QuantPlane layout) and a
-// per-column (or single) scale: src/sim_device.cc:541-602 and the epilogue of
+// C[m, n] = epilogue(scale[n] * sum_k A[m, k] * q[k, n]) with A fp32 [m, k], q int8
+// [k, n] (n contiguous: the reference's QuantPlane layout) and a per-column
+// (or single) scale: src/sim_device.cc:541-602 and the epilogue of
 // src/runtime.cc:332-344.
 //
-// Operand preparation happens in shared memory, per 64-deep k block:
-//  * q: int8 -> bf16 is exact (|q| <= 128 needs 8 significant bits), stored
-//    n-contiguous ("MN-major") in the 128-byte-swizzled canonical layout.
-//  * A: each fp32 value is split into three bf16 terms hi + mid + lo (each
-//    the rounded remainder of the previous), which carry the 24-bit fp32
-//    significand; products with the exact bf16 weight are exact, so three
-//    MMAs accumulating in fp32 reproduce the fp32 product to within the fp32
-//    accumulation error.
-// The MMA is issued "swapped": its M = 128 runs over output features (the
-// weight tile) and its N = R over activation rows, so decode with 32 rows is a
-// full-width MMA. D lives in TMEM (R fp32 columns); four warps read it back
-// with tcgen05.ld, one output feature per thread, and store rows coalesced.
+// Arithmetic. int8 -> bf16 is exact (|q| <= 128 needs 8 significant bits).
+// Each fp32 activation is split once into three bf16 planes hi + mid + lo
+// (each the rounded remainder of the previous); together they carry the
+// 24-bit fp32 significand, every product with the bf16 weight is exact, and
+// three MMAs per k step accumulate in fp32 in TMEM. The MMA is issued
+// "swapped": M = 128 runs over output features and N = R over activation rows,
+// so decode with 32 rows is a full-width MMA.
+//
+// Pipeline (one CTA = one 128-feature x R-row tile over a range of 64-deep k
+// blocks; 6 warps):
+//   warp 0  producer: per k block, one TMA of the raw int8 weight block
+//           [64 k x 128 n] and one TMA of the three activation planes
+//           [3 x R x 64 k] with 128-byte swizzle, which is already the MMA's
+//           K-major canonical layout; a ring of raw stages.
+//   warps 2-5 converters: int8 -> bf16 (integer and fp32-add bit arithmetic,
+//           exact) into the MMA's n-contiguous swizzled layout (two buffers);
+//           afterwards the epilogue: tcgen05.ld of the accumulator into a
+//           shared tile, then scale, fused epilogue and coalesced row stores.
+//   warp 1  MMA issuer (one thread): 3 planes x 4 k steps per block, then
+//           tcgen05.commit to the barriers that free the stage and buffer.
 // K can be split across CTAs; each split writes a partial tile and the last
-// CTA of a tile sums the partials in split order, so the result does not
-// depend on arrival order.
+// CTA of a tile sums the partials in split order (arrival order never changes
+// the result). Every mbarrier wait is bounded (tma.cuh).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <mutex>
+#include <string>
 
 #include "accel_b200.h"
 #include "common.cuh"
@@ -35,206 +46,270 @@ namespace accel_b200 {
 
 namespace {
 
-constexpr int kTcThreads = 128;
-constexpr int kBk = 64;                     // k per block: 128 bytes of bf16, one swizzle row
-constexpr int kBn = 128;                    // output features per tile (MMA M)
-constexpr int kATile = kBn * kBk * 2;       // 16 KB
-constexpr int kMmaK = 16;                   // k per bf16 MMA
+constexpr int kBk = 64;                // k per block: 128 bytes of bf16, one swizzle row
+constexpr int kBn = 128;               // output features per tile (MMA M)
+constexpr int kMmaK = 16;              // k per bf16 MMA
+constexpr int kWRaw = kBk * kBn;       // raw int8 weight block, 8 KiB
+constexpr int kWConv = kBk * kBn * 2;  // converted bf16 weight block, 16 KiB
+constexpr int kConvBufs = 2;
+constexpr int kConvWarps = 4;
+constexpr int kThreads = (2 + kConvWarps) * 32;
+constexpr int kMaxStages = 4;
+
+template <int R>
+struct Tc {
+  static constexpr int kXBytes = 3 * R * kBk * 2;    // three bf16 planes
+  static constexpr int kStage = kXBytes + kWRaw;     // planes first: 1024-aligned
+  static constexpr int kStages = R <= 64 ? 4 : 3;
+  static constexpr int kSmem = kStages * kStage + kConvBufs * kWConv + 1024;
+  static_assert(kStages <= kMaxStages, "stage count");
+};
 
 struct TcArgs {
-  const float* a;
-  int64_t lda;
-  const int8_t* w;
+  int64_t m, k, n;
+  int32_t kb_total;
+  int32_t kb_per_split;
   const float* scale;
   int32_t scalar_scale;
   float* c;
   int64_t ldc;
-  int64_t m, k, n;
-  int32_t kb_total;
-  int32_t kb_per_split;
   float* part;        // [splits][m][n] raw sums, splits > 1
   int32_t* counters;  // [row tiles][feature tiles]; zero before and after
   int32_t* status;
   Epilogue ep;
 };
 
-template <int R>
-struct TcLayout {
-  static constexpr int kBTile = R * kBk * 2;  // one bf16 term of the activations
-  static constexpr int kStage = kATile + 3 * kBTile;
-  static constexpr int kSmem = 2 * kStage + 1024;  // + slack to 1024-align the base
-};
+__device__ __forceinline__ void MbarArrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void TmaLoad2D(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          SmemAddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(SmemAddr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          SmemAddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(SmemAddr(bar))
+      : "memory");
+}
 
 __device__ __forceinline__ uint32_t PackBf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Weight block [64 k x 128 n] -> bf16, n-contiguous, 128-byte swizzle. Atom
-// (k / 8, n / 64) of 8 k rows x 128 bytes sits at (k/8) * 2048 + (n/64) * 1024;
-// the 16-byte chunk (n % 64) / 8 of row k % 8 is stored at chunk ^ (k % 8).
-__device__ __forceinline__ void LoadWeightBlock(const TcArgs& g, uint8_t* a_tile, int64_t k0, int64_t n0, int tid) {
+// Four int8 in a word -> two bf16x2 words, exactly and with full-rate integer
+// and fp32 adds only: XOR 0x80 turns each byte into q + 128 (offset binary);
+// a byte permute places it under the fp32 exponent of 2^23, so the float is
+// 2^23 + 128 + q; subtracting 2^23 + 128 leaves q exactly, and an integer-valued
+// float of at most 8 significant bits has a zero low half, so its top 16 bits
+// are the bf16 encoding.
+__device__ __forceinline__ void Int8x4ToBf16(uint32_t w, uint32_t* lo, uint32_t* hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+  *lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+  *hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+}
+
+// Raw weight block [64 k][128 n] int8 (dense rows of 128 bytes) -> bf16 in the
+// n-contiguous 128-byte-swizzled layout: atom (k / 8, n / 64) of 8 k rows x 128
+// bytes at (k / 8) * 2048 + (n / 64) * 1024; 16-byte chunk (n % 64) / 8 of row
+// k % 8 stored at chunk ^ (k % 8).
+__device__ __forceinline__ void ConvertWeightBlock(const uint8_t* raw, uint8_t* conv, int ct) {
 #pragma unroll
   for (int pass = 0; pass < 4; ++pass) {
-    const int idx = pass * kTcThreads + tid;
+    const int idx = pass * (kConvWarps * 32) + ct;
     const int kl = idx >> 3;
     const int nl = (idx & 7) * 16;
-    const int64_t gk = k0 + kl, gn = n0 + nl;
-    int8_t q[16];
-    if (gk < g.k && gn + 16 <= g.n) {
-      *reinterpret_cast<int4*>(q) = __ldg(reinterpret_cast<const int4*>(g.w + gk * g.n + gn));
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) q[i] = (gk < g.k && gn + i < g.n) ? g.w[gk * g.n + gn + i] : 0;
-    }
-    uint32_t packed[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) packed[i] = PackBf16(static_cast<float>(q[2 * i]), static_cast<float>(q[2 * i + 1]));
+    const uint4 q = *reinterpret_cast<const uint4*>(raw + kl * kBn + nl);
+    uint32_t p[8];
+    Int8x4ToBf16(q.x, &p[0], &p[1]);
+    Int8x4ToBf16(q.y, &p[2], &p[3]);
+    Int8x4ToBf16(q.z, &p[4], &p[5]);
+    Int8x4ToBf16(q.w, &p[6], &p[7]);
     const int row = kl & 7;
-    uint8_t* atom = a_tile + (kl >> 3) * 2048 + (nl >> 6) * 1024 + row * 128;
+    uint8_t* atom = conv + (kl >> 3) * 2048 + (nl >> 6) * 1024 + row * 128;
     const int chunk = (nl & 63) >> 3;
-    *reinterpret_cast<uint4*>(atom + (((chunk) ^ row) << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    *reinterpret_cast<uint4*>(atom + (((chunk + 1) ^ row) << 4)) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-  }
-}
-
-// Activation block [R rows x 64 k] -> three bf16 terms, k-contiguous, 128-byte
-// swizzle: row r at (r / 8) * 1024 + (r % 8) * 128, chunk (k / 8) ^ (r % 8).
-template <int R>
-__device__ __forceinline__ void LoadActBlock(const TcArgs& g, uint8_t* b_tiles, int64_t row0, int64_t k0, int tid) {
-  constexpr int kBTile = TcLayout<R>::kBTile;
-#pragma unroll
-  for (int pass = 0; pass < R / 8; ++pass) {
-    const int idx = pass * kTcThreads + tid;
-    const int rl = idx >> 4;
-    const int kl = (idx & 15) * 4;
-    const int64_t gr = row0 + rl, gk = k0 + kl;
-    float x[4];
-    if (gr < g.m && gk + 4 <= g.k) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(g.a + gr * g.lda + gk));
-      x[0] = v.x;
-      x[1] = v.y;
-      x[2] = v.z;
-      x[3] = v.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = (gr < g.m && gk + i < g.k) ? g.a[gr * g.lda + gk + i] : 0.f;
-    }
-    float hi[4], mid[4], lo[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      hi[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
-      const float r1 = x[i] - hi[i];
-      mid[i] = __bfloat162float(__float2bfloat16_rn(r1));
-      lo[i] = r1 - mid[i];
-    }
-    const int row = rl & 7;
-    const int off = (rl >> 3) * 1024 + row * 128 + ((((kl >> 3) ^ row)) << 4) + (kl & 7) * 2;
-    *reinterpret_cast<uint2*>(b_tiles + off) = make_uint2(PackBf16(hi[0], hi[1]), PackBf16(hi[2], hi[3]));
-    *reinterpret_cast<uint2*>(b_tiles + kBTile + off) = make_uint2(PackBf16(mid[0], mid[1]), PackBf16(mid[2], mid[3]));
-    *reinterpret_cast<uint2*>(b_tiles + 2 * kBTile + off) = make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+    *reinterpret_cast<uint4*>(atom + ((chunk ^ row) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+    *reinterpret_cast<uint4*>(atom + (((chunk + 1) ^ row) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
   }
 }
 
 template <int R>
-__global__ void __launch_bounds__(kTcThreads, 1) Q8GemmTcKernel(TcArgs g) {
-  using L = TcLayout<R>;
+__global__ void __launch_bounds__(kThreads, 1)
+    Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, TcArgs g) {
+  using L = Tc<R>;
+  constexpr int S = L::kStages;
+  // The three activation planes are 3R consecutive K-major rows in shared
+  // memory: one MMA with N = 3R covers all of them when 3R <= 256 and reads the
+  // weight operand once; D column p * R + r then holds plane p of row r.
+  constexpr bool kOneMma = 3 * R <= 256;
+  constexpr uint32_t kCols = 3 * R <= 128 ? 128 : (3 * R <= 256 ? 256 : 512);
+  constexpr uint32_t kIdesc = InstrDescBf16(kOneMma ? 3 * R : R, true);
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t mma_bar[2];
-  __shared__ uint32_t tmem_base_s;
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], cfull[kConvBufs], cempty[kConvBufs], accf;
+  __shared__ uint32_t tmem_s;
   __shared__ int32_t last_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t raw_addr = SmemAddr(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
+  uint8_t* conv_base = smem + S * L::kStage;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kBn;
   const int64_t row0 = static_cast<int64_t>(blockIdx.z) * R;
   const int kb_begin = blockIdx.y * g.kb_per_split;
-  const int kb_end = min(g.kb_total, kb_begin + g.kb_per_split);
-  const int nkb = max(0, kb_end - kb_begin);
-  constexpr uint32_t kCols = R < 32 ? 32 : R;
-  constexpr uint32_t kIdesc = InstrDescBf16(R, true);
+  const int nkb = max(0, min(g.kb_total, kb_begin + g.kb_per_split) - kb_begin);
 
-  if (warp == 0) TmemAlloc(&tmem_base_s, kCols);
+  if (warp == 1) TmemAlloc(&tmem_s, kCols);
   if (tid == 0) {
-    MbarInit(&mma_bar[0], 1);
-    MbarInit(&mma_bar[1], 1);
+    for (int s = 0; s < S; ++s) {
+      MbarInit(&full[s], 1);
+      MbarInit(&empty[s], 1 + kConvWarps);
+    }
+    for (int c = 0; c < kConvBufs; ++c) {
+      MbarInit(&cfull[c], kConvWarps);
+      MbarInit(&cempty[c], 1);
+    }
+    MbarInit(&accf, 1);
     FenceBarrierInit();
   }
   TcFenceBeforeSync();
   __syncthreads();
   TcFenceAfterSync();
-  const uint32_t tmem = tmem_base_s;
+  const uint32_t tmem = tmem_s;
   bool ok = true;
 
-  for (int i = 0; i < nkb; ++i) {
-    const int s = i & 1;
-    uint8_t* stage = smem + s * L::kStage;
-    if (i >= 2) ok &= MbarWait(&mma_bar[s], ((i >> 1) - 1) & 1);  // the MMAs that read this stage are done
-    const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBk;
-    LoadWeightBlock(g, stage, k0, n0, tid);
-    LoadActBlock<R>(g, stage + kATile, row0, k0, tid);
-    FenceProxyAsyncSmem();
-    __syncthreads();
-    if (tid == 0) {
-      TcFenceAfterSync();
-      const uint32_t a_addr = SmemAddr(stage);
-      const uint32_t b_addr = a_addr + kATile;
-#pragma unroll
-      for (int ks = 0; ks < kBk / kMmaK; ++ks) {
-        // A: two k atoms (16 k) per MMA, 4096 bytes; n atoms 1024 apart (LBO),
-        // k atoms 2048 apart (SBO). B: 32 bytes of k per MMA inside the
-        // swizzled row; 8-row groups 1024 apart (SBO).
-        const uint64_t adesc = SmemDescSw128(a_addr + ks * 4096, 1024, 2048);
-#pragma unroll
-        for (int part = 0; part < 3; ++part) {
-          const uint64_t bdesc = SmemDescSw128(b_addr + part * L::kBTile + ks * 32, 16, 1024);
-          MmaBf16(tmem, adesc, bdesc, kIdesc, (i | ks | part) != 0);
-        }
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        ok &= MbarWait(&empty[s], ((i / S) & 1) ^ 1);
+        uint8_t* stage = smem + s * L::kStage;
+        const int32_t k0 = (kb_begin + i) * kBk;
+        MbarArriveExpectTx(&full[s], L::kStage);
+        TmaLoad3D(stage, &tx, k0, static_cast<int32_t>(row0), 0, &full[s]);
+        TmaLoad2D(stage + L::kXBytes, &tw, static_cast<int32_t>(n0), k0, &full[s]);
       }
-      MmaCommit(&mma_bar[s]);
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S, c = i % kConvBufs;
+        ok &= MbarWait(&full[s], (i / S) & 1);
+        ok &= MbarWait(&cfull[c], (i / kConvBufs) & 1);
+        TcFenceAfterSync();
+        const uint32_t a_addr = SmemAddr(conv_base + c * kWConv);
+        const uint32_t b_addr = SmemAddr(smem + s * L::kStage);
+#pragma unroll
+        for (int ks = 0; ks < kBk / kMmaK; ++ks) {
+          // A (weights, n-contiguous): 16 k = two k atoms = 4096 bytes per step;
+          // n atoms 1024 apart (LBO), k atoms 2048 apart (SBO). B (planes,
+          // k-contiguous): 32 bytes of k per step inside the swizzled row;
+          // 8-row groups 1024 apart (SBO); planes R * 128 bytes apart.
+          const uint64_t adesc = SmemDescSw128(a_addr + ks * 4096, 1024, 2048);
+          if constexpr (kOneMma) {
+            MmaBf16(tmem, adesc, SmemDescSw128(b_addr + ks * 32, 16, 1024), kIdesc, (i | ks) != 0);
+          } else {
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+              const uint64_t bdesc = SmemDescSw128(b_addr + p * R * 128 + ks * 32, 16, 1024);
+              MmaBf16(tmem + p * R, adesc, bdesc, kIdesc, (i | ks) != 0);
+            }
+          }
+        }
+        MmaCommit(&empty[s]);
+        MmaCommit(&cempty[c]);
+      }
+      if (nkb > 0) MmaCommit(&accf);
+    }
+  } else {
+    const int ct = tid - 64;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % S, c = i % kConvBufs;
+      ok &= MbarWait(&full[s], (i / S) & 1);
+      ok &= MbarWait(&cempty[c], ((i / kConvBufs) & 1) ^ 1);
+      ConvertWeightBlock(smem + s * L::kStage + L::kXBytes, conv_base + c * kWConv, ct);
+      FenceProxyAsyncSmem();
+      __syncwarp();
+      if (lane == 0) {
+        MbarArrive(&cfull[c]);
+        MbarArrive(&empty[s]);
+      }
+    }
+    if (nkb > 0) ok &= MbarWait(&accf, 0);
   }
-  if (nkb > 0) ok &= MbarWait(&mma_bar[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1);
   if (!__syncthreads_and(ok)) {
-    // A wait ran out: report it, give the tensor core one more bounded wait
-    // before the TMEM is released, and leave the output untouched.
+    // A wait ran out: report it, let the tensor core finish (bounded), free
+    // the TMEM and leave the output untouched.
     if (tid == 0 && g.status != nullptr) atomicOr(g.status, ACCEL_B200_STATUS_COPY_TIMEOUT);
-    if (nkb > 0) MbarWait(&mma_bar[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1);
+    if (nkb > 0) MbarWait(&accf, 0);
     TcFenceBeforeSync();
     __syncthreads();
-    if (warp == 0) TmemDealloc(tmem, kCols);
+    if (warp == 1) TmemDealloc(tmem, kCols);
     return;
   }
   TcFenceAfterSync();
-
-  const int64_t gn = n0 + warp * 32 + lane;
-  const bool col_ok = gn < g.n;
-  const float sc = g.scalar_scale ? __ldg(g.scale) : (col_ok ? __ldg(g.scale + gn) : 0.f);
   const bool split = gridDim.y > 1;
+  const int64_t rows = Min64(R, g.m - row0);
+  const int64_t cols = Min64(kBn, g.n - n0);
+  if (warp >= 2) {
+    // Accumulator -> shared tile [R][128] fp32 (the stage memory is idle now),
+    // then one compact loop applies the scale and epilogue and stores rows.
+    float* tile = reinterpret_cast<float*>(smem);
+    const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. +31
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+    for (int c0 = 0; c0 < R; c0 += 32) {
+      float v[32];
+      if (nkb > 0) {
+        // hi + mid + lo, each accumulated separately over K.
+        float w[32];
+        TmemLoad32(lane_base + c0, v);
+        TmemLoad32(lane_base + R + c0, w);
 #pragma unroll
-  for (int c0 = 0; c0 < R; c0 += 32) {
-    float v[32];
-    if (nkb > 0) {
-      TmemLoad32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-    } else {
+        for (int j = 0; j < 32; ++j) v[j] += w[j];
+        TmemLoad32(lane_base + 2 * R + c0, w);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    }
-    if (!col_ok) continue;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int64_t row = row0 + c0 + j;
-      if (row >= g.m) break;
-      if (split) {
-        g.part[(static_cast<int64_t>(blockIdx.y) * g.m + row) * g.n + gn] = v[j];
+        for (int j = 0; j < 32; ++j) v[j] += w[j];
       } else {
-        g.c[row * g.ldc + gn] = ApplyEpilogue(g.ep, __fmul_rn(v[j], sc), row, gn);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) tile[(c0 + j) * kBn + quarter * 32 + lane] = v[j];
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+    // Thread et owns column et of the tile for every row.
+    const int et = tid - 64;
+    const int64_t col = n0 + et;
+    if (et < cols) {
+      const float sc = split ? 1.f : (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col));
+#pragma unroll 4
+      for (int64_t r = 0; r < rows; ++r) {
+        const int64_t row = row0 + r;
+        const float val = tile[r * kBn + et];
+        if (split) {
+          g.part[(static_cast<int64_t>(blockIdx.y) * g.m + row) * g.n + col] = val;
+        } else {
+          g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(val, sc), row, col);
+        }
       }
     }
   }
   TcFenceBeforeSync();
   __syncthreads();
-  if (warp == 0) TmemDealloc(tmem, kCols);
+  if (warp == 1) TmemDealloc(tmem, kCols);
   if (!split) return;
 
   // Split K: the last CTA of this tile sums the partials in split order.
@@ -245,23 +320,61 @@ __global__ void __launch_bounds__(kTcThreads, 1) Q8GemmTcKernel(TcArgs g) {
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  const int64_t rows = Min64(R, g.m - row0);
-  const int64_t cols = Min64(kBn, g.n - n0);
-  for (int64_t idx = tid; idx < rows * cols; idx += kTcThreads) {
+  const int splits = static_cast<int>(gridDim.y);
+  const int64_t plane = g.m * g.n;
+#pragma unroll 1
+  for (int64_t idx = tid; idx < rows * cols; idx += kThreads) {
     const int64_t row = row0 + idx / cols, col = n0 + idx % cols;
+    const float* p = g.part + row * g.n + col;
     float sum = 0.f;
-    for (int p = 0; p < static_cast<int>(gridDim.y); ++p) sum += __ldcg(g.part + (p * g.m + row) * g.n + col);
+    int q = 0;
+    for (; q + 4 <= splits; q += 4) {
+      const float a0 = __ldcg(p + (q + 0) * plane), a1 = __ldcg(p + (q + 1) * plane);
+      const float a2 = __ldcg(p + (q + 2) * plane), a3 = __ldcg(p + (q + 3) * plane);
+      sum += a0;
+      sum += a1;
+      sum += a2;
+      sum += a3;
+    }
+    for (; q < splits; ++q) sum += __ldcg(p + q * plane);
     const float s2 = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
     g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(sum, s2), row, col);
   }
   if (tid == 0) *counter = 0;
 }
 
+// fp32 [m, k] (row stride lda) -> three bf16 planes [3][m][k]: hi = bf16(x),
+// mid = bf16(x - hi), lo = bf16(x - hi - mid).
+__global__ void SplitPlanesKernel(const float* __restrict__ a, int64_t lda, int64_t m, int64_t k,
+                                  __nv_bfloat16* __restrict__ planes) {
+  const int64_t quads = k / 4;
+  const int64_t total = m * quads;
+  const int64_t plane = m * k;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / quads, q = idx - r * quads;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(a + r * lda + q * 4));
+    const float x[4] = {v.x, v.y, v.z, v.w};
+    float hi[4], mid[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      hi[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
+      const float r1 = x[i] - hi[i];
+      mid[i] = __bfloat162float(__float2bfloat16_rn(r1));
+      lo[i] = r1 - mid[i];
+    }
+    const int64_t off = r * k + q * 4;
+    *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(hi[0], hi[1]), PackBf16(hi[2], hi[3]));
+    *reinterpret_cast<uint2*>(planes + plane + off) = make_uint2(PackBf16(mid[0], mid[1]), PackBf16(mid[2], mid[3]));
+    *reinterpret_cast<uint2*>(planes + 2 * plane + off) = make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+  }
+}
+
 struct TcPlan {
   int r;
   int64_t feature_tiles, row_tiles;
   int32_t kb_total, kb_per_split, splits;
-  size_t counter_bytes, part_bytes;
+  size_t planes_bytes, part_bytes;
 };
 
 TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n) {
@@ -270,77 +383,129 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n) {
   p.feature_tiles = CeilDiv(n, kBn);
   p.row_tiles = CeilDiv(m, p.r);
   p.kb_total = static_cast<int32_t>(CeilDiv(k, kBk));
+  // Split K only when each CTA would otherwise walk a long K with few tiles in
+  // the grid: aim for about one wave of CTAs and at least 8 k blocks per split.
   const int64_t base = p.feature_tiles * p.row_tiles;
-  int64_t want = CeilDiv(2 * kSms, base);
-  if (want > p.kb_total) want = p.kb_total;
+  int64_t want = 1;
+  if (base < kSms && p.kb_total > 16) {
+    want = CeilDiv(kSms, base);
+    const int64_t by_depth = p.kb_total / 8;
+    if (want > by_depth) want = by_depth;
+  }
   if (want < 1 || base > kMaxCounters) want = 1;  // split K needs one counter per tile
   p.kb_per_split = static_cast<int32_t>(CeilDiv(p.kb_total, want));
   p.splits = static_cast<int32_t>(CeilDiv(p.kb_total, p.kb_per_split));
-  p.counter_bytes = kCounterRegion;
+  p.planes_bytes = (static_cast<size_t>(3) * m * k * 2 + 1023) / 1024 * 1024;
   p.part_bytes = p.splits > 1 ? static_cast<size_t>(p.splits) * m * n * sizeof(float) : 0;
   return p;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 EncodeFn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      ptr = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
 template <int R>
-int LaunchTc(const TcArgs& g, const TcPlan& p, cudaStream_t s) {
+int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
   static std::once_flag once[16];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 15], [] {
-    cudaFuncSetAttribute(Q8GemmTcKernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<R>::kSmem);
+    cudaFuncSetAttribute(Q8GemmTcKernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tc<R>::kSmem);
   });
   Q8GemmTcKernel<R><<<dim3(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
                            static_cast<unsigned>(p.row_tiles)),
-                      kTcThreads, TcLayout<R>::kSmem, s>>>(g);
+                      kThreads, Tc<R>::kSmem, s>>>(tw, tx, g);
   return CheckLaunch("matmul_q8_tc");
 }
 
 }  // namespace
 
 // Whether the tensor-core path takes this product: a per-column or single
-// scale without zero points, 16-byte aligned rows of A and of the weight.
+// scale without zero points; weight rows a multiple of 16 bytes and
+// activation rows a multiple of 8 elements (TMA strides); 16-byte aligned.
 bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
                 int64_t n) {
   if (zero != nullptr || (axis != 1 && axis != -1)) return false;
-  if (m <= 0 || k <= 0 || n <= 0 || n % 16 != 0 || lda % 4 != 0) return false;
+  if (m <= 0 || k <= 0 || n <= 0 || n % 16 != 0 || k % 8 != 0 || lda % 4 != 0) return false;
   if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0) return false;
-  const int64_t row_tiles = CeilDiv(m, m <= 32 ? 32 : (m <= 64 ? 64 : 128));
-  return row_tiles <= 65535 && CeilDiv(n, kBn) <= 2147483647LL;
+  if (k > (int64_t{1} << 31) - 1 || n > (int64_t{1} << 31) - 1 || m > (int64_t{1} << 31) - 1) return false;
+  return CeilDiv(m, m <= 32 ? 32 : (m <= 64 ? 64 : 128)) <= 65535 && EncodeFn() != nullptr;
 }
 
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
   const TcPlan p = MakeTcPlan(m, k, n);
-  return p.counter_bytes + p.part_bytes;
+  return kCounterRegion + p.planes_bytes + p.part_bytes;
 }
 
 int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c, int64_t ldc,
           int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace, size_t workspace_bytes,
           int32_t* status, cudaStream_t stream) {
   const TcPlan p = MakeTcPlan(m, k, n);
-  if (workspace == nullptr || workspace_bytes < p.counter_bytes + p.part_bytes) {
+  if (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes + p.part_bytes) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
   }
+  char* ws = static_cast<char*>(workspace);
+  auto* planes = reinterpret_cast<__nv_bfloat16*>(ws + kCounterRegion);
+  {
+    const int64_t total = m * (k / 4);
+    const int64_t blocks = CeilDiv(total, 256);
+    const int grid = static_cast<int>(blocks < kSms * 16 ? blocks : kSms * 16);
+    SplitPlanesKernel<<<grid, 256, 0, stream>>>(a, lda, m, k, planes);
+    const int rc = CheckLaunch("matmul_q8_split");
+    if (rc != ACCEL_B200_OK) return rc;
+  }
+  PFN_cuTensorMapEncodeTiled_v12000 encode = EncodeFn();
+  CUtensorMap tw{}, tx{};
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(k)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(n)};
+    const cuuint32_t box[2] = {kBn, kBk};
+    const cuuint32_t estr[2] = {1, 1};
+    if (encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      return SetError(ACCEL_B200_EINVAL, "matmul_q8: weight tensor map rejected");
+    }
+  }
+  {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m), 3};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) * 2, static_cast<cuuint64_t>(m) * k * 2};
+    const cuuint32_t box[3] = {kBk, static_cast<cuuint32_t>(p.r), 3};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (encode(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, planes, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      return SetError(ACCEL_B200_EINVAL, "matmul_q8: activation tensor map rejected");
+    }
+  }
   TcArgs g{};
-  g.a = a;
-  g.lda = lda;
-  g.w = w;
-  g.scale = scale;
-  g.scalar_scale = scalar_scale ? 1 : 0;
-  g.c = c;
-  g.ldc = ldc;
   g.m = m;
   g.k = k;
   g.n = n;
   g.kb_total = p.kb_total;
   g.kb_per_split = p.kb_per_split;
-  g.counters = static_cast<int32_t*>(workspace);
-  g.part = p.part_bytes > 0 ? reinterpret_cast<float*>(static_cast<char*>(workspace) + p.counter_bytes) : nullptr;
+  g.scale = scale;
+  g.scalar_scale = scalar_scale ? 1 : 0;
+  g.c = c;
+  g.ldc = ldc;
+  g.counters = reinterpret_cast<int32_t*>(ws);
+  g.part = p.part_bytes > 0 ? reinterpret_cast<float*>(ws + kCounterRegion + p.planes_bytes) : nullptr;
   g.status = status;
   g.ep = ep;
   switch (p.r) {
-    case 32: return LaunchTc<32>(g, p, stream);
-    case 64: return LaunchTc<64>(g, p, stream);
-    default: return LaunchTc<128>(g, p, stream);
+    case 32: return LaunchTc<32>(tw, tx, g, p, stream);
+    case 64: return LaunchTc<64>(tw, tx, g, p, stream);
+    default: return LaunchTc<128>(tw, tx, g, p, stream);
   }
 }
 

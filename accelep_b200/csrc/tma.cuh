@@ -11,9 +11,11 @@
 
 namespace accel_b200 {
 
-// Upper bound on the wait for one mbarrier phase: one second of the global
-// timer, far beyond any real copy latency (microseconds).
-constexpr uint64_t kWaitLimitNs = 1000000000ull;
+// Upper bound on the wait for one mbarrier phase: 2^31 SM clock cycles (about
+// one second at 1.9 GHz, under two at the lowest clocks), far beyond any real
+// copy or MMA latency (microseconds). The cycle counter is cheap to read,
+// unlike the global timer, and is read only after a run of failed polls.
+constexpr long long kWaitLimitCycles = 1ll << 31;
 
 __device__ __forceinline__ uint64_t GlobalTimerNs() {
   uint64_t t;
@@ -47,11 +49,14 @@ __device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t
       : "memory");
 }
 
+// Non-blocking test of phase `parity`: the waiting thread is never suspended,
+// so a completed phase is seen on the next poll (a suspended try_wait adds a
+// wake-up delay to every hand-off of a pipeline).
 __device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
       : "r"(SmemAddr(bar)), "r"(parity)
@@ -61,12 +66,13 @@ __device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
 
 // Waits for phase `parity` of `bar` to complete; false when the bound ran out.
 __device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
-  const uint64_t start = GlobalTimerNs();
+  if (MbarTryWait(bar, parity)) return true;
+  const long long start = clock64();
   for (;;) {
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < 256; ++i) {
       if (MbarTryWait(bar, parity)) return true;
     }
-    if (GlobalTimerNs() - start > kWaitLimitNs) return false;
+    if (clock64() - start > kWaitLimitCycles) return false;
   }
 }
 

@@ -1,0 +1,117 @@
+"""Times single kernels of the backend on fixed cases, for profiling.
+
+    python -m accelep_b200.profile_cases gemm [--path tc|simt] [--shapes decode|prefill|c5|all]
+    python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280]
+    python -m accelep_b200.profile_cases list
+
+Each case is launched `reps` times from one captured CUDA graph (no host
+overhead between launches), after warm-up, and timed with CUDA events on the
+capturing stream. Several input copies are rotated so that each launch reads
+its operands from HBM rather than L2. The same commands run under ncu for the
+summaries in profiles/.
+"""
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from . import kernels as K
+from . import synthetic as syn
+
+GEMM_SHAPES = {
+    "decode": [("qkv", 32, 576, 960), ("o", 32, 576, 576), ("gate_up", 32, 576, 3072), ("down", 32, 1536, 576),
+               ("lm_head", 32, 576, 49152)],
+    "prefill": [("p_qkv", 16384, 576, 960), ("p_gate_up", 16384, 576, 3072), ("p_down", 16384, 1536, 576)],
+    "c5": [("c5_m1_k4096", 1, 4096, 4096), ("c5_m16_k4096", 16, 4096, 4096), ("c5_m1_k16384", 1, 16384, 16384),
+           ("c5_m16_k16384", 16, 16384, 16384), ("c5_m128_k8192", 128, 8192, 8192),
+           ("c5_m2048_k8192", 2048, 8192, 8192)],
+}
+
+
+def _time_graph(launch, reps, stream):
+    """Captures `reps` calls of launch(i) into one graph; returns us per call."""
+    for i in range(3):
+        launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(reps):
+            launch(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    graph.replay()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) * 1000.0 / reps
+
+
+def gemm_case(name, m, k, n, reps, copies=None):
+    """int8 product C = A @ dequant(W) at one shape; returns a result row."""
+    weight_bytes = k * n
+    copies = copies or max(1, min(8, int(np.ceil(300e6 / max(weight_bytes, 1)))))
+    x, w, s = syn.int8_gemm(m, k, n, 1)
+    xs = torch.from_numpy(x).cuda()
+    ws_ = [torch.from_numpy(w).cuda() for _ in range(copies)]
+    st = torch.from_numpy(s).cuda()
+    out = torch.zeros(m, n, device="cuda")
+    need = K.load().accel_b200_matmul_q8_workspace(m, k, n)
+    work = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        us = _time_graph(lambda i: K.matmul_q8(xs, ws_[i % copies], st, out=out, workspace=work), reps, stream)
+    nbytes = k * n + 4 * n + 4 * m * k + 4 * m * n
+    return {"case": name, "m": m, "k": k, "n": n, "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
+            "tflops": round(2 * m * k * n / us / 1e6, 2), "weight_copies": copies}
+
+
+def attention_case(batch, length, reps, context=2048, heads=9, kv_heads=3, head_dim=64):
+    copies = 4
+    kc = [torch.randn(batch, kv_heads, context, head_dim, device="cuda") for _ in range(copies)]
+    vc = [torch.randn(batch, kv_heads, context, head_dim, device="cuda") for _ in range(copies)]
+    q = torch.randn(batch, heads * head_dim, device="cuda")
+    lens = torch.full((batch,), length, dtype=torch.int32, device="cuda")
+    work = K.attention_decode_workspace(batch, heads, kv_heads, context)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        us = _time_graph(lambda i: K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kv_heads,
+                                                      head_dim, context, head_major=True, workspace=work),
+                         reps, stream)
+    nbytes = batch * length * 2 * kv_heads * head_dim * 4 + 2 * batch * heads * head_dim * 4
+    return {"case": f"attention_decode_b{batch}_len{length}", "us": round(us, 3),
+            "gbs": round(nbytes / us / 1e3, 1)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "attention", "list"])
+    ap.add_argument("--path", default="tc", choices=["tc", "simt"])
+    ap.add_argument("--shapes", default="decode", choices=["decode", "prefill", "c5", "all"])
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--len", type=int, default=1280)
+    ap.add_argument("--reps", type=int, default=50)
+    ap.add_argument("--only", default="", help="run one named gemm case")
+    args = ap.parse_args()
+    if args.what == "list":
+        print(json.dumps(GEMM_SHAPES))
+        return
+    torch.cuda.set_device(0)
+    if args.what == "gemm":
+        K.set_q8_path(1 if args.path == "simt" else 0)
+        groups = list(GEMM_SHAPES) if args.shapes == "all" else [args.shapes]
+        for group in groups:
+            for name, m, k, n in GEMM_SHAPES[group]:
+                if args.only and name != args.only:
+                    continue
+                reps = args.reps if m * k * n < 1e10 else max(3, args.reps // 10)
+                print(json.dumps(dict(gemm_case(name, m, k, n, reps), path=args.path)), flush=True)
+        K.set_q8_path(0)
+    else:
+        print(json.dumps(attention_case(args.batch, args.len, args.reps)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
