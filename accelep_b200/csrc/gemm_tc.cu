@@ -25,9 +25,11 @@
 //           shared tile, then scale, fused epilogue and coalesced row stores.
 //   warp 1  MMA issuer (one thread): 3 planes x 4 k steps per block, then
 //           tcgen05.commit to the barriers that free the stage and buffer.
-// K can be split across CTAs; each split writes a partial tile and the last
-// CTA of a tile sums the partials in split order (arrival order never changes
-// the result). Every mbarrier wait is bounded (tma.cuh).
+// K can be split across the CTAs of one thread-block cluster (up to 8); each
+// keeps its partial tile in shared memory and the cluster sums the tiles in
+// rank order through distributed shared memory, so the result is
+// deterministic and no partial sums go to global memory. Every mbarrier wait
+// is bounded (tma.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -56,12 +58,14 @@ constexpr int kConvWarps = 4;
 constexpr int kThreads = (2 + kConvWarps) * 32;
 constexpr int kMaxStages = 4;
 
-template <int R>
+template <int R, int S>
 struct Tc {
   static constexpr int kXBytes = 3 * R * kBk * 2;    // three bf16 planes
   static constexpr int kStage = kXBytes + kWRaw;     // planes first: 1024-aligned
-  static constexpr int kStages = R <= 64 ? 4 : 3;
-  static constexpr int kSmem = kStages * kStage + kConvBufs * kWConv + 1024;
+  static constexpr int kStages = S;
+  static constexpr int kTile = R * kBn * 4;          // fp32 accumulator tile, staged in stage memory
+  static constexpr int kStageArea = kStages * kStage > kTile ? kStages * kStage : kTile;
+  static constexpr int kSmem = kStageArea + kConvBufs * kWConv + 1024;
   static_assert(kStages <= kMaxStages, "stage count");
 };
 
@@ -73,11 +77,35 @@ struct TcArgs {
   int32_t scalar_scale;
   float* c;
   int64_t ldc;
-  float* part;        // [splits][m][n] raw sums, splits > 1
-  int32_t* counters;  // [row tiles][feature tiles]; zero before and after
   int32_t* status;
   Epilogue ep;
 };
+
+__device__ __forceinline__ void ClusterSync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The same shared-memory offset in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t PeerAddr(const void* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(SmemAddr(local)), "r"(rank));
+  return remote;
+}
+
+__device__ __forceinline__ float4 LoadPeer4(const float* local, uint32_t rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(PeerAddr(local, rank))
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int32_t LoadPeerInt(const int32_t* local, uint32_t rank) {
+  int32_t v;
+  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(PeerAddr(local, rank)) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void MbarArrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar)) : "memory");
@@ -145,10 +173,10 @@ __device__ __forceinline__ void ConvertWeightBlock(const uint8_t* raw, uint8_t* 
   }
 }
 
-template <int R>
+template <int R, int kStagesT>
 __global__ void __launch_bounds__(kThreads, 1)
     Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, TcArgs g) {
-  using L = Tc<R>;
+  using L = Tc<R, kStagesT>;
   constexpr int S = L::kStages;
   // The three activation planes are 3R consecutive K-major rows in shared
   // memory: one MMA with N = 3R covers all of them when 3R <= 256 and reads the
@@ -159,11 +187,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], cfull[kConvBufs], cempty[kConvBufs], accf;
   __shared__ uint32_t tmem_s;
-  __shared__ int32_t last_s;
+  __shared__ int32_t ok_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t raw_addr = SmemAddr(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
-  uint8_t* conv_base = smem + S * L::kStage;
+  uint8_t* conv_base = smem + L::kStageArea;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kBn;
   const int64_t row0 = static_cast<int64_t>(blockIdx.z) * R;
   const int kb_begin = blockIdx.y * g.kb_per_split;
@@ -249,24 +277,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (nkb > 0) ok &= MbarWait(&accf, 0);
   }
-  if (!__syncthreads_and(ok)) {
-    // A wait ran out: report it, let the tensor core finish (bounded), free
-    // the TMEM and leave the output untouched.
+  const bool cta_ok = __syncthreads_and(ok);
+  if (!cta_ok) {
+    // A wait ran out: report it and let the tensor core finish (bounded). The
+    // CTA still takes part in the cluster barriers below, so that no peer
+    // waits for it, but the tile is not written.
     if (tid == 0 && g.status != nullptr) atomicOr(g.status, ACCEL_B200_STATUS_COPY_TIMEOUT);
     if (nkb > 0) MbarWait(&accf, 0);
-    TcFenceBeforeSync();
-    __syncthreads();
-    if (warp == 1) TmemDealloc(tmem, kCols);
-    return;
   }
+  if (tid == 0) ok_s = cta_ok ? 1 : 0;
   TcFenceAfterSync();
-  const bool split = gridDim.y > 1;
+  // Split K runs as one thread-block cluster along grid y; every CTA of the
+  // cluster holds its partial tile in shared memory and the cluster sums the
+  // tiles in rank order (deterministic) through distributed shared memory.
+  const int splits = static_cast<int>(gridDim.y);
   const int64_t rows = Min64(R, g.m - row0);
   const int64_t cols = Min64(kBn, g.n - n0);
-  if (warp >= 2) {
-    // Accumulator -> shared tile [R][128] fp32 (the stage memory is idle now),
-    // then one compact loop applies the scale and epilogue and stores rows.
-    float* tile = reinterpret_cast<float*>(smem);
+  float* tile = reinterpret_cast<float*>(smem);  // [R][128] fp32; the stage memory is idle now
+  if (warp >= 2 && cta_ok) {
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. +31
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
@@ -289,58 +317,65 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 32; ++j) tile[(c0 + j) * kBn + quarter * 32 + lane] = v[j];
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
-    // Thread et owns column et of the tile for every row.
-    const int et = tid - 64;
-    const int64_t col = n0 + et;
-    if (et < cols) {
-      const float sc = split ? 1.f : (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col));
-#pragma unroll 4
-      for (int64_t r = 0; r < rows; ++r) {
-        const int64_t row = row0 + r;
-        const float val = tile[r * kBn + et];
-        if (split) {
-          g.part[(static_cast<int64_t>(blockIdx.y) * g.m + row) * g.n + col] = val;
-        } else {
-          g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(val, sc), row, col);
-        }
-      }
-    }
   }
   TcFenceBeforeSync();
   __syncthreads();
   if (warp == 1) TmemDealloc(tmem, kCols);
-  if (!split) return;
-
-  // Split K: the last CTA of this tile sums the partials in split order.
-  __threadfence();
-  __syncthreads();
-  int32_t* counter = g.counters + static_cast<int64_t>(blockIdx.z) * gridDim.x + blockIdx.x;
-  if (tid == 0) last_s = atomicAdd(counter, 1) == static_cast<int32_t>(gridDim.y) - 1;
-  __syncthreads();
-  if (!last_s) return;
-  __threadfence();
-  const int splits = static_cast<int>(gridDim.y);
-  const int64_t plane = g.m * g.n;
-#pragma unroll 1
-  for (int64_t idx = tid; idx < rows * cols; idx += kThreads) {
-    const int64_t row = row0 + idx / cols, col = n0 + idx % cols;
-    const float* p = g.part + row * g.n + col;
-    float sum = 0.f;
-    int q = 0;
-    for (; q + 4 <= splits; q += 4) {
-      const float a0 = __ldcg(p + (q + 0) * plane), a1 = __ldcg(p + (q + 1) * plane);
-      const float a2 = __ldcg(p + (q + 2) * plane), a3 = __ldcg(p + (q + 3) * plane);
-      sum += a0;
-      sum += a1;
-      sum += a2;
-      sum += a3;
+  if (splits == 1) {
+    // Thread t < 128 owns column t of the tile for every row.
+    if (cta_ok && tid < cols) {
+      const int64_t col = n0 + tid;
+      const float sc = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
+#pragma unroll 4
+      for (int64_t r = 0; r < rows; ++r) {
+        const int64_t row = row0 + r;
+        g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
+      }
     }
-    for (; q < splits; ++q) sum += __ldcg(p + q * plane);
-    const float s2 = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
-    g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(sum, s2), row, col);
+    return;
   }
-  if (tid == 0) *counter = 0;
+  ClusterSync();  // every partial tile (and ok flag) of the cluster is complete
+  bool all_ok = true;
+  for (int p = 0; p < splits; ++p) all_ok &= LoadPeerInt(&ok_s, static_cast<uint32_t>(p)) != 0;
+  if (all_ok) {
+    // The tile's rows * 32 groups of four columns are dealt out to the cluster
+    // in contiguous ranges; each group is summed over ranks 0, 1, ... in order.
+    const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
+    const int groups = static_cast<int>(rows) * (kBn / 4);
+    const int per = (groups + splits - 1) / splits;
+    const int g_end = min(groups, (rank + 1) * per);
+#pragma unroll 1
+    for (int idx = rank * per + tid; idx < g_end; idx += kThreads) {
+      const int r = idx >> 5, c4 = (idx & 31) * 4;
+      if (c4 >= cols) continue;
+      const float* src = tile + r * kBn + c4;
+      float4 part[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < splits) part[q] = LoadPeer4(src, static_cast<uint32_t>(q));
+      float4 sum = part[0];
+#pragma unroll
+      for (int q = 1; q < 8; ++q) {
+        if (q < splits) {
+          sum.x += part[q].x;
+          sum.y += part[q].y;
+          sum.z += part[q].z;
+          sum.w += part[q].w;
+        }
+      }
+      const float v[4] = {sum.x, sum.y, sum.z, sum.w};
+      const int64_t row = row0 + r;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t col = n0 + c4 + j;
+        if (c4 + j < cols) {
+          const float sc = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
+          g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(v[j], sc), row, col);
+        }
+      }
+    }
+  }
+  ClusterSync();  // no CTA leaves while a peer may still read its tile
 }
 
 // fp32 [m, k] (row stride lda) -> three bf16 planes [3][m][k]: hi = bf16(x),
@@ -372,9 +407,10 @@ __global__ void SplitPlanesKernel(const float* __restrict__ a, int64_t lda, int6
 
 struct TcPlan {
   int r;
+  int stages;
   int64_t feature_tiles, row_tiles;
   int32_t kb_total, kb_per_split, splits;
-  size_t planes_bytes, part_bytes;
+  size_t planes_bytes;
 };
 
 TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n) {
@@ -383,20 +419,19 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n) {
   p.feature_tiles = CeilDiv(n, kBn);
   p.row_tiles = CeilDiv(m, p.r);
   p.kb_total = static_cast<int32_t>(CeilDiv(k, kBk));
-  // Split K only when each CTA would otherwise walk a long K with few tiles in
-  // the grid: aim for about one wave of CTAs and at least 8 k blocks per split.
+  // When the tile grid is smaller than the GPU, split K across a cluster of up
+  // to 8 CTAs, aiming at about two CTAs per SM and at least two k blocks per
+  // CTA (a CTA's hand-offs per k block, not bandwidth, bound small products).
   const int64_t base = p.feature_tiles * p.row_tiles;
-  int64_t want = 1;
-  if (base < kSms && p.kb_total > 16) {
-    want = CeilDiv(kSms, base);
-    const int64_t by_depth = p.kb_total / 8;
-    if (want > by_depth) want = by_depth;
+  int64_t splits = 1;
+  if (base < kSms && p.kb_total > 1) {
+    splits = Min64(CeilDiv(p.kb_total, 2), CeilDiv(2 * kSms, base));
+    if (splits > 8) splits = 8;
   }
-  if (want < 1 || base > kMaxCounters) want = 1;  // split K needs one counter per tile
-  p.kb_per_split = static_cast<int32_t>(CeilDiv(p.kb_total, want));
+  p.kb_per_split = static_cast<int32_t>(CeilDiv(p.kb_total, splits));
   p.splits = static_cast<int32_t>(CeilDiv(p.kb_total, p.kb_per_split));
+  p.stages = p.kb_per_split <= 2 ? 2 : (p.r <= 64 ? 4 : 3);
   p.planes_bytes = (static_cast<size_t>(3) * m * k * 2 + 1023) / 1024 * 1024;
-  p.part_bytes = p.splits > 1 ? static_cast<size_t>(p.splits) * m * n * sizeof(float) : 0;
   return p;
 }
 
@@ -414,18 +449,43 @@ PFN_cuTensorMapEncodeTiled_v12000 EncodeFn() {
   return fn;
 }
 
-template <int R>
+template <int R, int ST>
 int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
   static std::once_flag once[16];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 15], [] {
-    cudaFuncSetAttribute(Q8GemmTcKernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tc<R>::kSmem);
+    cudaFuncSetAttribute(Q8GemmTcKernel<R, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tc<R, ST>::kSmem);
   });
-  Q8GemmTcKernel<R><<<dim3(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
-                           static_cast<unsigned>(p.row_tiles)),
-                      kThreads, Tc<R>::kSmem, s>>>(tw, tx, g);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
+                     static_cast<unsigned>(p.row_tiles));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Tc<R, ST>::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(p.splits);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, Q8GemmTcKernel<R, ST>, tw, tx, g);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return SetError(ACCEL_B200_ECUDA, std::string("matmul_q8_tc: ") + cudaGetErrorString(err));
+  }
   return CheckLaunch("matmul_q8_tc");
+}
+
+template <int R>
+int LaunchTcStages(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
+  if (p.stages == 2) return LaunchTc<R, 2>(tw, tx, g, p, s);
+  if constexpr (R <= 64) {
+    return LaunchTc<R, 4>(tw, tx, g, p, s);
+  } else {
+    return LaunchTc<R, 3>(tw, tx, g, p, s);
+  }
 }
 
 }  // namespace
@@ -444,14 +504,14 @@ bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, cons
 
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
   const TcPlan p = MakeTcPlan(m, k, n);
-  return kCounterRegion + p.planes_bytes + p.part_bytes;
+  return kCounterRegion + p.planes_bytes;
 }
 
 int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c, int64_t ldc,
           int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace, size_t workspace_bytes,
           int32_t* status, cudaStream_t stream) {
   const TcPlan p = MakeTcPlan(m, k, n);
-  if (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes + p.part_bytes) {
+  if (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
   }
   char* ws = static_cast<char*>(workspace);
@@ -498,14 +558,12 @@ int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool
   g.scalar_scale = scalar_scale ? 1 : 0;
   g.c = c;
   g.ldc = ldc;
-  g.counters = reinterpret_cast<int32_t*>(ws);
-  g.part = p.part_bytes > 0 ? reinterpret_cast<float*>(ws + kCounterRegion + p.planes_bytes) : nullptr;
   g.status = status;
   g.ep = ep;
   switch (p.r) {
-    case 32: return LaunchTc<32>(tw, tx, g, p, stream);
-    case 64: return LaunchTc<64>(tw, tx, g, p, stream);
-    default: return LaunchTc<128>(tw, tx, g, p, stream);
+    case 32: return LaunchTcStages<32>(tw, tx, g, p, stream);
+    case 64: return LaunchTcStages<64>(tw, tx, g, p, stream);
+    default: return LaunchTcStages<128>(tw, tx, g, p, stream);
   }
 }
 

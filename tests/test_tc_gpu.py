@@ -1,7 +1,8 @@
 """The tcgen05 int8 product (accel_b200_matmul_q8 on its tensor-core path)
 against the CPU checker and against the CUDA-core path: partial feature
 tiles, partial row tiles, K that is not a multiple of the 64-deep block,
-split K, single scales and the fused epilogue."""
+split K across a thread-block cluster (with a ragged last split), single
+scales and the fused epilogue."""
 
 import numpy as np
 import pytest
@@ -37,7 +38,8 @@ def by_shape():
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 64, 128), (32, 576, 960), (7, 100, 336), (33, 576, 576), (64, 1536, 576),
-                                   (100, 192, 3072), (130, 576, 1536), (300, 640, 272), (32, 1536, 49152)])
+                                   (100, 192, 3072), (130, 576, 1536), (300, 640, 272), (32, 1536, 49152),
+                                   (5, 4104, 256), (128, 8192, 512)])
 def test_tc_matches_checker(lib, cuda, orc, m, k, n):
     x, w, s = syn.int8_gemm(m, k, n, m + k + n)
     res = np.random.default_rng(m).standard_normal((m, n), dtype=np.float32)
