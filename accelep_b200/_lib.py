@@ -73,6 +73,8 @@ SIGNATURES = {
     "accel_b200_attention_decode_noalloc_limit": (c_sz, []),
     "accel_b200_attention_decode_noalloc": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_i32,
                                                     c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp]),
+    "accel_b200_decode_attention": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
+                                            c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]),
     "accel_b200_silu_mul_rows": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "accel_b200_sample_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_f32, c_vp, c_i32, c_vp]),
     "accel_b200_greedy_step": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32,

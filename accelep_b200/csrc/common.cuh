@@ -83,4 +83,15 @@ __device__ __forceinline__ float ApplyEpilogue(const Epilogue& ep, float acc, in
   return v;
 }
 
+// Rotate-half RoPE of one pair (src/sim_rope.cc:16-17): x[i] and x[half + i] of a
+// head with the position's cos/sin rows `c`, `s` (head_dim entries each):
+//   lo = x[i] * c[i] - x[half + i] * s[i]
+//   hi = x[half + i] * c[half + i] + x[i] * s[half + i]
+// every step a rounded float operation, as the reference evaluates it.
+__device__ __forceinline__ void RopePair(float a, float b, const float* c, const float* s, int i, int half, float* lo,
+                                         float* hi) {
+  *lo = __fsub_rn(__fmul_rn(a, c[i]), __fmul_rn(b, s[i]));
+  *hi = __fadd_rn(__fmul_rn(b, c[half + i]), __fmul_rn(a, s[half + i]));
+}
+
 }  // namespace accel_b200

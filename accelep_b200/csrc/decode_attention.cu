@@ -1,0 +1,361 @@
+// One decode step of a layer's attention for a batch of sequences, fused:
+// RoPE of the new query and key rows (src/sim_rope.cc:16-17), the append of
+// the new key and value rows to the cache (src/sim_cache.cc) and causal
+// grouped-query attention over the whole context (src/sim_attend.cc:9-46),
+// as Generate runs them per token (src/llama_model.cc:229-233).
+//
+// Layout. The cache is head-major: slot b, kv head g, position t at
+// k_cache + b * seq_stride + g * head_stride + t * 64 (floats), so the rows of
+// one (sequence, kv head) are one contiguous block. head_dim is 64.
+//
+// Work split. One thread-block cluster of S CTAs per (sequence, kv head); the
+// context's 64-row chunks are dealt to the S ranks in contiguous ranges. A
+// CTA streams its chunks through two shared-memory buffers with bulk copies
+// (the next chunk is in flight while the current one is scored), keeps an
+// online softmax (running max, sum and weighted values) for the G query heads
+// of its kv head, and publishes that state in shared memory. The cluster then
+// merges the S states in rank order through distributed shared memory
+// (log-sum-exp rule), so the result does not depend on scheduling and no
+// workspace or counters are needed. The rank whose range holds the new row
+// computes it (RoPE on the key), writes it to the cache and places it in its
+// buffer instead of copying it.
+//
+// Rows with position < 0 (finished sequences) do nothing. Every mbarrier wait
+// is bounded; a wait that runs out sets ACCEL_B200_STATUS_COPY_TIMEOUT and the
+// CTA still reaches the cluster barriers.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+
+#include "accel_b200.h"
+#include "cluster.cuh"
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace accel_b200 {
+namespace {
+
+constexpr int kD = 64;          // head_dim
+constexpr int kRows = 64;       // context rows per chunk
+constexpr int kThreads = 128;
+constexpr int kMaxG = 8;        // query heads per kv head
+constexpr int kMaxSplit = 8;    // CTAs per cluster
+constexpr int kChunkFloats = kRows * kD;
+constexpr int kSmemBytes = 2 * 2 * kChunkFloats * 4;  // two buffers of K and V
+
+struct FusedArgs {
+  const float* qkv;  // row r: heads * 64 query | kv_heads * 64 key | kv_heads * 64 value (before RoPE)
+  int64_t qkv_ld;
+  const int32_t* row_seq;  // cache slot of row r; null: slot r
+  const int32_t* row_pos;  // position of row r's token; < 0: finished, skipped
+  const float* cos_t;      // [context][64]
+  const float* sin_t;
+  float* k_cache;
+  float* v_cache;
+  int64_t seq_stride;
+  int64_t head_stride;
+  int32_t heads;
+  int32_t kv_heads;
+  int32_t context;
+  float scale;
+  float* out;  // row r: heads * 64 at out + r * out_ld
+  int64_t out_ld;
+  int32_t* status;
+};
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a) {
+  extern __shared__ __align__(128) float buf[];  // [2][K | V][64 rows][64]
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ __align__(16) float qs[G * kD];  // roped query heads
+  __shared__ __align__(16) float ps[G * kRows];  // scores, then weights, of the current chunk
+  __shared__ __align__(16) float mo[G * kD];  // published weighted values
+  __shared__ float m_run[G], l_run[G], corr[G];
+  __shared__ int32_t ok_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rank = static_cast<int>(blockIdx.x), S = static_cast<int>(gridDim.x);
+  const int g = static_cast<int>(blockIdx.y);
+  const int64_t r = blockIdx.z;
+  const int64_t pos = a.row_pos[r];
+  const int h0 = g * G;
+
+  // The chunk range of this rank.
+  const int64_t len = pos + 1;
+  const int used = pos >= 0 ? static_cast<int>((len + kRows - 1) / kRows) : 0;
+  const int per = (used + S - 1) / S;
+  const int c_begin = min(used, rank * per), c_end = min(used, c_begin + per);
+  const int nloc = c_end - c_begin;
+  const int64_t slot = a.row_seq != nullptr ? a.row_seq[r] : r;
+  float* kbase = a.k_cache + slot * a.seq_stride + g * a.head_stride;
+  float* vbase = a.v_cache + slot * a.seq_stride + g * a.head_stride;
+  const float* row = a.qkv + r * a.qkv_ld;
+
+  if (tid == 0) {
+    MbarInit(&full[0], 1);
+    MbarInit(&full[1], 1);
+    FenceBarrierInit();
+  }
+  if (tid < G) {
+    m_run[tid] = -INFINITY;
+    l_run[tid] = 0.f;
+  }
+  __syncthreads();
+
+  // Issues the copies of local chunk i into buffer i & 1. The new row (the
+  // last of the context) is not copied: the owner writes it.
+  auto issue = [&](int i) {
+    const int64_t t0 = static_cast<int64_t>(c_begin + i) * kRows;
+    const int64_t cnt = Min64(kRows, len - t0);
+    const int64_t copy = t0 + cnt == len ? cnt - 1 : cnt;
+    float* kb = buf + (i & 1) * 2 * kChunkFloats;
+    uint64_t* bar = &full[i & 1];
+    if (copy > 0) {
+      const uint32_t bytes = static_cast<uint32_t>(copy) * kD * 4;
+      MbarArriveExpectTx(bar, 2 * bytes);
+      BulkCopyG2S(kb, kbase + t0 * kD, bytes, bar);
+      BulkCopyG2S(kb + kChunkFloats, vbase + t0 * kD, bytes, bar);
+    } else {
+      MbarArrive(bar);
+    }
+  };
+  if (tid == 0) {
+    if (nloc > 0) issue(0);
+    if (nloc > 1) issue(1);
+  }
+
+  // RoPE of the G query heads into shared memory (all ranks need them).
+  if (pos >= 0) {
+    const float* c = a.cos_t + pos * kD;
+    const float* s = a.sin_t + pos * kD;
+    for (int p = tid; p < G * (kD / 2); p += kThreads) {
+      const int hh = p / (kD / 2), i = p % (kD / 2);
+      const float* x = row + static_cast<int64_t>(h0 + hh) * kD;
+      float lo, hi;
+      RopePair(x[i], x[kD / 2 + i], c, s, i, kD / 2, &lo, &hi);
+      qs[hh * kD + i] = lo;
+      qs[hh * kD + kD / 2 + i] = hi;
+    }
+  }
+  __syncthreads();
+
+  // Weighted values: thread (d = tid % 64, half = tid / 64) owns heads
+  // half, half + 2, ... of dimension d.
+  const int d = tid & (kD - 1), vh = tid >> 6;
+  float acc[(G + 1) / 2];
+#pragma unroll
+  for (int j = 0; j < (G + 1) / 2; ++j) acc[j] = 0.f;
+  bool ok = true;
+
+  for (int i = 0; i < nloc; ++i) {
+    float* kb = buf + (i & 1) * 2 * kChunkFloats;
+    float* vb = kb + kChunkFloats;
+    const int64_t t0 = static_cast<int64_t>(c_begin + i) * kRows;
+    const int cnt = static_cast<int>(Min64(kRows, len - t0));
+    ok &= MbarWait(&full[i & 1], (i >> 1) & 1);
+    if (t0 + cnt == len) {
+      // The new row: RoPE on its key, append key and value to the cache, and
+      // place both in the buffer as row cnt - 1.
+      const float* c = a.cos_t + pos * kD;
+      const float* s = a.sin_t + pos * kD;
+      const float* kin = row + static_cast<int64_t>(a.heads + g) * kD;
+      const float* vin = row + static_cast<int64_t>(a.heads + a.kv_heads + g) * kD;
+      if (tid < kD / 2) {
+        float lo, hi;
+        RopePair(kin[tid], kin[kD / 2 + tid], c, s, tid, kD / 2, &lo, &hi);
+        kb[(cnt - 1) * kD + tid] = lo;
+        kb[(cnt - 1) * kD + kD / 2 + tid] = hi;
+        kbase[pos * kD + tid] = lo;
+        kbase[pos * kD + kD / 2 + tid] = hi;
+      } else if (tid >= 64) {
+        const float v = vin[tid - 64];
+        vb[(cnt - 1) * kD + tid - 64] = v;
+        vbase[pos * kD + tid - 64] = v;
+      }
+      __syncthreads();
+    }
+    // Scores: two threads per row, each over half of the dimensions; the
+    // float4 index rotates with the row so a quarter-warp hits 32 banks.
+    {
+      const int j = tid >> 1, half = tid & 1;
+      const bool valid = j < cnt;
+      float dot[G];
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) dot[hh] = 0.f;
+      if (valid) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int d4 = half * 8 + ((q + j + 4 * half) & 7);
+          const float4 kv = *reinterpret_cast<const float4*>(kb + j * kD + d4 * 4);
+#pragma unroll
+          for (int hh = 0; hh < G; ++hh) {
+            const float4 qv = *reinterpret_cast<const float4*>(qs + hh * kD + d4 * 4);
+            dot[hh] = fmaf(qv.x, kv.x, dot[hh]);
+            dot[hh] = fmaf(qv.y, kv.y, dot[hh]);
+            dot[hh] = fmaf(qv.z, kv.z, dot[hh]);
+            dot[hh] = fmaf(qv.w, kv.w, dot[hh]);
+          }
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) {
+        const float other = __shfl_xor_sync(kFull, dot[hh], 1);
+        if (valid && half == 0) ps[hh * kRows + j] = (dot[hh] + other) * a.scale;
+      }
+    }
+    __syncthreads();
+    // Online softmax per head: new max, weights of this chunk, rescale factor.
+    for (int hh = warp; hh < G; hh += kThreads / 32) {
+      float mx = -INFINITY;
+      for (int j = lane; j < cnt; j += 32) mx = fmaxf(mx, ps[hh * kRows + j]);
+      mx = fmaxf(WarpMax(mx), m_run[hh]);
+      float sum = 0.f;
+      for (int j = lane; j < cnt; j += 32) {
+        const float p = expf(ps[hh * kRows + j] - mx);
+        ps[hh * kRows + j] = p;
+        sum += p;
+      }
+      sum = WarpSum(sum);
+      if (lane == 0) {
+        const float f = expf(m_run[hh] - mx);  // 0 on the first chunk
+        corr[hh] = f;
+        l_run[hh] = l_run[hh] * f + sum;
+        m_run[hh] = mx;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < (G + 1) / 2; ++j) {
+      const int hh = vh + 2 * j;
+      if (hh < G) {
+        const float* p = ps + hh * kRows;
+        float o = 0.f;
+        for (int t = 0; t < cnt; ++t) o = fmaf(p[t], vb[t * kD + d], o);
+        acc[j] = acc[j] * corr[hh] + o;
+      }
+    }
+    __syncthreads();  // buffer i & 1 and the weights are free
+    if (tid == 0 && i + 2 < nloc) issue(i + 2);
+  }
+  ok = __syncthreads_and(ok);
+  if (!ok) {
+    if (tid == 0 && a.status != nullptr) atomicOr(a.status, ACCEL_B200_STATUS_COPY_TIMEOUT);
+    // Copies still in flight land before the CTA leaves (bounded waits).
+    for (int i = 0; i < nloc && i < 2; ++i) MbarWait(&full[i & 1], ((nloc - 1 - i) >> 1) & 1);
+  }
+#pragma unroll
+  for (int j = 0; j < (G + 1) / 2; ++j) {
+    const int hh = vh + 2 * j;
+    if (hh < G) mo[hh * kD + d] = acc[j];
+  }
+  if (tid == 0) ok_s = ok ? 1 : 0;
+  ClusterSync();  // every rank's state is published
+  bool all_ok = true;
+  for (int p = 0; p < S; ++p) all_ok &= LoadPeerInt(&ok_s, static_cast<uint32_t>(p)) != 0;
+  if (all_ok && pos >= 0) {
+    // Rank `rank` merges outputs rank, rank + S, ... of the G * 64.
+    for (int e = rank * kThreads + tid; e < G * kD; e += S * kThreads) {
+      const int hh = e / kD;
+      float mx = -INFINITY;
+      for (int p = 0; p < S; ++p) mx = fmaxf(mx, LoadPeer(&m_run[hh], static_cast<uint32_t>(p)));
+      float l = 0.f, o = 0.f;
+      for (int p = 0; p < S; ++p) {
+        const float w = expf(LoadPeer(&m_run[hh], static_cast<uint32_t>(p)) - mx);
+        l = fmaf(LoadPeer(&l_run[hh], static_cast<uint32_t>(p)), w, l);
+        o = fmaf(LoadPeer(&mo[e], static_cast<uint32_t>(p)), w, o);
+      }
+      a.out[r * a.out_ld + static_cast<int64_t>(h0) * kD + e] = o / l;
+    }
+  }
+  ClusterSync();  // no CTA leaves while a peer may still read its state
+}
+
+// CTAs per cluster: about 2.5 CTAs per SM over the whole grid, at most one
+// per chunk of the longest context and at most 8.
+int SplitFor(int64_t rows, int32_t kv_heads, int32_t context) {
+  const int64_t pairs = rows * kv_heads;
+  int64_t s = CeilDiv(5 * kSms / 2, pairs);
+  s = Min64(s, CeilDiv(context, kRows));
+  return static_cast<int>(Max64(1, Min64(s, kMaxSplit)));
+}
+
+template <int G>
+int LaunchFused(const FusedArgs& a, int64_t rows, cudaStream_t stream) {
+  static std::once_flag once[16];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 15], [] {
+    cudaFuncSetAttribute(AttnDecodeFusedKernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  });
+  const int S = SplitFor(rows, a.kv_heads, a.context);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(S), static_cast<unsigned>(a.kv_heads), static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, AttnDecodeFusedKernel<G>, a);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return SetError(ACCEL_B200_ECUDA, std::string("decode_attention: ") + cudaGetErrorString(err));
+  }
+  return CheckLaunch("decode_attention");
+}
+
+}  // namespace
+}  // namespace accel_b200
+
+using namespace accel_b200;
+
+extern "C" {
+
+ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld, const int32_t* row_seq,
+                                               const int32_t* row_pos, int64_t rows, int32_t heads, int32_t kv_heads,
+                                               int32_t head_dim, const float* cos_table, const float* sin_table,
+                                               int32_t context, float* k_cache, float* v_cache, int64_t seq_stride,
+                                               int64_t head_stride, float* out, int64_t out_ld, int32_t* status,
+                                               void* stream) {
+  if (rows < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim != kD || context <= 0 ||
+      qkv == nullptr || row_pos == nullptr || cos_table == nullptr || sin_table == nullptr || k_cache == nullptr ||
+      v_cache == nullptr || out == nullptr) {
+    return SetError(ACCEL_B200_EINVAL, "decode_attention: bad arguments (head_dim must be 64)");
+  }
+  if (rows == 0) return ClearError();
+  if (rows > 65535) return SetError(ACCEL_B200_EINVAL, "decode_attention: more than 65535 rows");
+  if (qkv_ld < static_cast<int64_t>(heads + 2 * kv_heads) * kD || out_ld < static_cast<int64_t>(heads) * kD) {
+    return SetError(ACCEL_B200_EINVAL, "decode_attention: row strides too small");
+  }
+  if (head_stride < static_cast<int64_t>(context) * kD || seq_stride < head_stride * kv_heads) {
+    return SetError(ACCEL_B200_EINVAL, "decode_attention: cache strides do not hold the context");
+  }
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0 || seq_stride % 4 != 0 ||
+      head_stride % 4 != 0) {
+    return SetError(ACCEL_B200_EINVAL, "decode_attention: cache rows must be 16-byte aligned");
+  }
+  const int group = heads / kv_heads;
+  if (group > kMaxG) return SetError(ACCEL_B200_EINVAL, "decode_attention: more than 8 query heads per kv head");
+  FusedArgs a{qkv,     qkv_ld,  row_seq,    row_pos,     cos_table, sin_table, k_cache,
+              v_cache, seq_stride, head_stride, heads, kv_heads,  context,   1.f / sqrtf(static_cast<float>(kD)),
+              out,     out_ld,  status};
+  cudaStream_t s = AsStream(stream);
+  switch (group) {
+    case 1: return LaunchFused<1>(a, rows, s);
+    case 2: return LaunchFused<2>(a, rows, s);
+    case 3: return LaunchFused<3>(a, rows, s);
+    case 4: return LaunchFused<4>(a, rows, s);
+    case 5: return LaunchFused<5>(a, rows, s);
+    case 6: return LaunchFused<6>(a, rows, s);
+    case 7: return LaunchFused<7>(a, rows, s);
+    default: return LaunchFused<8>(a, rows, s);
+  }
+}
+
+}  // extern "C"

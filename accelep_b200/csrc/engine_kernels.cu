@@ -23,12 +23,6 @@
 namespace accel_b200 {
 namespace {
 
-__device__ __forceinline__ void RotatePair(float a, float b, const float* c, const float* s, int i, int half, float* lo,
-                                           float* hi) {
-  *lo = __fsub_rn(__fmul_rn(a, c[i]), __fmul_rn(b, s[i]));
-  *hi = __fadd_rn(__fmul_rn(b, c[half + i]), __fmul_rn(a, s[half + i]));
-}
-
 // One CTA per row. Query pairs are rotated in place; key pairs are rotated
 // into the cache; value rows are copied into the cache.
 __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int32_t* __restrict__ row_seq,
@@ -52,7 +46,7 @@ __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int3
     const int h = p / half, i = p % half;
     float* x = row + h * head_dim;
     float lo, hi;
-    RotatePair(x[i], x[half + i], c, s, i, half, &lo, &hi);
+    RopePair(x[i], x[half + i], c, s, i, half, &lo, &hi);
     x[i] = lo;
     x[half + i] = hi;
   }
@@ -61,7 +55,7 @@ __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int3
     const int h = p / half, i = p % half;
     const float* x = kin + h * head_dim;
     float lo, hi;
-    RotatePair(x[i], x[half + i], c, s, i, half, &lo, &hi);
+    RopePair(x[i], x[half + i], c, s, i, half, &lo, &hi);
     kslot[h * head_stride + i] = lo;
     kslot[h * head_stride + half + i] = hi;
   }

@@ -40,6 +40,7 @@
 #include <string>
 
 #include "accel_b200.h"
+#include "cluster.cuh"
 #include "common.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
@@ -80,36 +81,6 @@ struct TcArgs {
   int32_t* status;
   Epilogue ep;
 };
-
-__device__ __forceinline__ void ClusterSync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// The same shared-memory offset in cluster CTA `rank`.
-__device__ __forceinline__ uint32_t PeerAddr(const void* local, uint32_t rank) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(SmemAddr(local)), "r"(rank));
-  return remote;
-}
-
-__device__ __forceinline__ float4 LoadPeer4(const float* local, uint32_t rank) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(PeerAddr(local, rank))
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ int32_t LoadPeerInt(const int32_t* local, uint32_t rank) {
-  int32_t v;
-  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(PeerAddr(local, rank)) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void MbarArrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar)) : "memory");
-}
 
 __device__ __forceinline__ void TmaLoad2D(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
   asm volatile(

@@ -569,8 +569,6 @@ class Engine {
       ws = std::max(ws, GemmWorkspace(lm_head, std::min<int64_t>(m, seqs)));
     }
     moved |= gemm_ws.Ensure(ws);
-    moved |= attn_ws.Ensure(
-        accel_b200_attention_decode_workspace(seqs, cfg.heads, cfg.kv_heads, cfg.context, kDecodeChunk));
     moved |= status.Ensure(16);
     if (moved) DropGraphs();
   }
@@ -624,15 +622,15 @@ class Engine {
       float* vc = v_cache[static_cast<size_t>(li)].as<float>();
       Abi(accel_b200_rmsnorm(hid, l.attn_norm.as<float>(), normed.as<float>(), rows, H, cfg.eps, 0, stream));
       Gemm(normed.as<float>(), H, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr);
-      Abi(accel_b200_rope_append(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
-                                 rope_cos.as<float>(), rope_sin.as<float>(), kc, vc, slot_stride, head_stride,
-                                 row_stride, stream));
       if (decode && head_dim == 64) {
-        Abi(accel_b200_attention_decode(qkv.as<float>(), qkv_ld, kc, vc, row_stride, head_stride, slot_stride,
-                                        lens.as<int32_t>(), seqs, cfg.heads, cfg.kv_heads, head_dim, cfg.context,
-                                        kDecodeChunk, mixed.as<float>(), q_out, attn_ws.p, attn_ws.bytes,
-                                        status.as<int32_t>(), stream));
+        // Rope, AppendCache and attention of the new rows in one kernel.
+        Abi(accel_b200_decode_attention(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
+                                        rope_cos.as<float>(), rope_sin.as<float>(), cfg.context, kc, vc, slot_stride,
+                                        head_stride, mixed.as<float>(), q_out, status.as<int32_t>(), stream));
       } else {
+        Abi(accel_b200_rope_append(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
+                                   rope_cos.as<float>(), rope_sin.as<float>(), kc, vc, slot_stride, head_stride,
+                                   row_stride, stream));
         Abi(accel_b200_attention_rows(qkv.as<float>(), qkv_ld, kc, vc, row_stride, head_stride, slot_stride,
                                       mixed.as<float>(), q_out, rseq, decode ? dec_len_pos() : rpos, rows, cfg.heads,
                                       cfg.kv_heads, head_dim, stream));
@@ -700,8 +698,6 @@ class Engine {
     }
   }
 
-  static constexpr int32_t kDecodeChunk = 64;
-
   DevBuf embed, final_norm, rope_cos, rope_sin;
   std::vector<Layer> layers;
   Group lm_head;
@@ -712,7 +708,7 @@ class Engine {
   DevBuf ids;
   int32_t ids_rows = 0;
   int64_t ids_stride = 0;
-  DevBuf gemm_ws, attn_ws, status;
+  DevBuf gemm_ws, status;
   PinnedBuf staging, finished_host;
   cudaGraphExec_t graph_exec = nullptr;
   std::tuple<int32_t, bool, float, int32_t, int32_t> graph_key;

@@ -194,6 +194,28 @@ def attention_decode(q, k_cache, v_cache, lens, heads, kv_heads, head_dim, max_l
     return out
 
 
+def rope_append(qkv, row_seq, row_pos, heads, kv_heads, head_dim, cos_t, sin_t, k_cache, v_cache):
+    """Rope + AppendCache over fused q|k|v rows (queries rotated in place).
+    Caches head-major [slots, kv_heads, context, head_dim]."""
+    ctx = k_cache.shape[2]
+    check(load().accel_b200_rope_append(_p(qkv), qkv.stride(0), _p(row_seq), _p(row_pos), qkv.shape[0], heads,
+                                        kv_heads, head_dim, _p(cos_t), _p(sin_t), _p(k_cache), _p(v_cache),
+                                        kv_heads * ctx * head_dim, ctx * head_dim, head_dim, _s()))
+
+
+def decode_attention(qkv, row_pos, heads, kv_heads, cos_t, sin_t, k_cache, v_cache, row_seq=None, out=None,
+                     status=None):
+    """Fused decode step (Rope, AppendCache, attention) over un-rotated q|k|v
+    rows; caches head-major [slots, kv_heads, context, 64]."""
+    rows, ctx = qkv.shape[0], k_cache.shape[2]
+    if out is None:
+        out = torch.zeros(rows, heads * 64, dtype=torch.float32, device=qkv.device)
+    check(load().accel_b200_decode_attention(_p(qkv), qkv.stride(0), _p(row_seq), _p(row_pos), rows, heads, kv_heads,
+                                             64, _p(cos_t), _p(sin_t), ctx, _p(k_cache), _p(v_cache),
+                                             kv_heads * ctx * 64, ctx * 64, _p(out), out.stride(0), _p(status), _s()))
+    return out
+
+
 def attention_decode_workspace(batch, heads, kv_heads, max_len, chunk=64, device="cuda"):
     """A zeroed workspace for attention_decode (its counters start at zero)."""
     need = load().accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk)

@@ -1,7 +1,7 @@
 """Times single kernels of the backend on fixed cases, for profiling.
 
     python -m accelep_b200.profile_cases gemm [--path tc|simt] [--shapes decode|prefill|c5|all]
-    python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280]
+    python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280] [--kind fused|split]
     python -m accelep_b200.profile_cases list
 
 Each case is launched `reps` times from one captured CUDA graph (no host
@@ -68,21 +68,34 @@ def gemm_case(name, m, k, n, reps, copies=None):
             "tflops": round(2 * m * k * n / us / 1e6, 2), "weight_copies": copies}
 
 
-def attention_case(batch, length, reps, context=2048, heads=9, kv_heads=3, head_dim=64):
+def attention_case(batch, length, reps, kind="fused", context=2048, heads=9, kv_heads=3, head_dim=64):
+    """Decode attention of `batch` sequences at context length `length` over
+    head-major caches: the fused step (Rope, AppendCache, attention) or the
+    split-KV kernel alone. Bytes counted: the key and value rows read."""
     copies = 4
     kc = [torch.randn(batch, kv_heads, context, head_dim, device="cuda") for _ in range(copies)]
     vc = [torch.randn(batch, kv_heads, context, head_dim, device="cuda") for _ in range(copies)]
-    q = torch.randn(batch, heads * head_dim, device="cuda")
-    lens = torch.full((batch,), length, dtype=torch.int32, device="cuda")
-    work = K.attention_decode_workspace(batch, heads, kv_heads, context)
     stream = torch.cuda.Stream()
-    with torch.cuda.stream(stream):
-        us = _time_graph(lambda i: K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kv_heads,
-                                                      head_dim, context, head_major=True, workspace=work),
-                         reps, stream)
-    nbytes = batch * length * 2 * kv_heads * head_dim * 4 + 2 * batch * heads * head_dim * 4
-    return {"case": f"attention_decode_b{batch}_len{length}", "us": round(us, 3),
-            "gbs": round(nbytes / us / 1e3, 1)}
+    if kind == "fused":
+        qkv = torch.randn(batch, (heads + 2 * kv_heads) * head_dim, device="cuda")
+        pos = torch.full((batch,), length - 1, dtype=torch.int32, device="cuda")
+        ang = torch.arange(context, dtype=torch.float64, device="cuda")[:, None] * torch.ones(head_dim, device="cuda",
+                                                                                              dtype=torch.float64)
+        cos_t, sin_t = torch.cos(ang * 1e-3).float(), torch.sin(ang * 1e-3).float()
+        out = torch.zeros(batch, heads * head_dim, device="cuda")
+        with torch.cuda.stream(stream):
+            us = _time_graph(lambda i: K.decode_attention(qkv, pos, heads, kv_heads, cos_t, sin_t, kc[i % copies],
+                                                          vc[i % copies], out=out), reps, stream)
+    else:
+        q = torch.randn(batch, heads * head_dim, device="cuda")
+        lens = torch.full((batch,), length, dtype=torch.int32, device="cuda")
+        work = K.attention_decode_workspace(batch, heads, kv_heads, context)
+        with torch.cuda.stream(stream):
+            us = _time_graph(lambda i: K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kv_heads,
+                                                          head_dim, context, head_major=True, workspace=work),
+                             reps, stream)
+    nbytes = batch * length * 2 * kv_heads * head_dim * 4
+    return {"case": f"attention_{kind}_b{batch}_len{length}", "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1)}
 
 
 def main():
@@ -93,6 +106,7 @@ def main():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--len", type=int, default=1280)
     ap.add_argument("--reps", type=int, default=50)
+    ap.add_argument("--kind", default="fused", choices=["fused", "split"])
     ap.add_argument("--only", default="", help="run one named gemm case")
     args = ap.parse_args()
     if args.what == "list":
@@ -110,7 +124,7 @@ def main():
                 print(json.dumps(dict(gemm_case(name, m, k, n, reps), path=args.path)), flush=True)
         K.set_q8_path(0)
     else:
-        print(json.dumps(attention_case(args.batch, args.len, args.reps)), flush=True)
+        print(json.dumps(attention_case(args.batch, args.len, args.reps, args.kind)), flush=True)
 
 
 if __name__ == "__main__":

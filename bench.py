@@ -177,9 +177,12 @@ def run_reference(args):
 # ------------------------------------------------------------------ B200 arm
 
 def attention_roofline(torch, stream, batch=SEQS, length=1280, reps=50):
-    """Times the split-KV decode attention launch alone at the workload's mean
+    """Times the engine's decode attention launch (Rope, AppendCache and
+    attention fused, accel_b200_decode_attention) alone at the workload's mean
     context (1280 rows) with CUDA events on the launching stream; returns
-    (algorithmic GB/s, seconds per launch, bytes per launch)."""
+    (algorithmic GB/s, seconds per launch, bytes per launch). Algorithmic
+    bytes: the key and value rows read, the new rows written, the q|k|v rows
+    read and the output written."""
     from accelep_b200 import kernels as K
 
     cfg = syn.SMOLLM2_135M
@@ -191,22 +194,28 @@ def attention_roofline(torch, stream, batch=SEQS, length=1280, reps=50):
         copies = 4
         kc = [torch.randn(batch, kvh, CONTEXT, hd, device="cuda") for _ in range(copies)]
         vc = [torch.randn(batch, kvh, CONTEXT, hd, device="cuda") for _ in range(copies)]
-        q = torch.randn(batch, heads * hd, device="cuda")
-        lens = torch.full((batch,), length, dtype=torch.int32, device="cuda")
-        ws = K.attention_decode_workspace(batch, heads, kvh, CONTEXT)
+        qkv = torch.randn(batch, (heads + 2 * kvh) * hd, device="cuda")
+        pos = torch.full((batch,), length - 1, dtype=torch.int32, device="cuda")
+        ang = torch.arange(CONTEXT, dtype=torch.float64, device="cuda")[:, None] * torch.ones(
+            hd, dtype=torch.float64, device="cuda") * 1e-3
+        cos_t, sin_t = torch.cos(ang).float(), torch.sin(ang).float()
+        out = torch.zeros(batch, heads * hd, device="cuda")
+
+        def launch(i):
+            K.decode_attention(qkv, pos, heads, kvh, cos_t, sin_t, kc[i % copies], vc[i % copies], out=out)
+
         for i in range(3):
-            K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kvh, hd, CONTEXT, head_major=True,
-                               workspace=ws)
+            launch(i)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         start.record(stream)
         for i in range(reps):
-            K.attention_decode(q, kc[i % copies], vc[i % copies], lens, heads, kvh, hd, CONTEXT, head_major=True,
-                               workspace=ws)
+            launch(i)
         end.record(stream)
         end.synchronize()
     sec = start.elapsed_time(end) / 1000.0 / reps
-    nbytes = batch * length * 2 * kvd * 4 + 2 * batch * heads * hd * 4
+    nbytes = batch * (length - 1) * 2 * kvd * 4 + batch * 2 * kvd * 4 + batch * (heads + 2 * kvh) * hd * 4 + \
+        batch * heads * hd * 4
     del kc, vc
     return nbytes / sec / 1e9, sec, nbytes
 
@@ -292,7 +301,8 @@ def run_b200(args):
                 "e2e": {"value": tokens / wall, "unit": UNIT, "h2d_bytes_per_step": SEQS * prompt_len * 4,
                         "d2h_bytes_per_step": SEQS * new * 4},
                 "gpu_launches": int(launches),
-                "roofline": {"kernel": "attention_decode (split-KV, B=32, 1280 context rows)", "bound": "hbm",
+                "roofline": {"kernel": "decode_attention (fused Rope+AppendCache+attention, B=32, 1280 context rows)",
+                             "bound": "hbm",
                              "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": None,
                              "bytes_per_launch": nbytes, "us_per_launch": sec * 1e6},

@@ -254,6 +254,28 @@ ACCEL_B200_API int accel_b200_attention_decode_noalloc(const float* q, int64_t q
                                                        int32_t max_len, int32_t chunk, float* out,
                                                        int64_t out_row_stride, int32_t* status, void* stream);
 
+/* One decode step of a layer's attention, fused (src/llama_model.cc:229-233
+   for one new token per sequence): Rope on the query and key heads of row r,
+   AppendCache of its key and value at position row_pos[r] of slot row_seq[r]
+   (row_seq may be NULL: slot r), and causal attention of the query heads over
+   cache rows [0, row_pos[r]] (src/sim_attend.cc:9-46). qkv rows as in
+   accel_b200_rope_append; qkv is only read (the rotated queries stay in
+   shared memory). head_dim 64; the cache must be head-major (row stride
+   64 floats): element (slot s, kv head g, row t, dim d) at s * seq_stride +
+   g * head_stride + t * 64 + d, head_stride >= context * 64. Rows with
+   row_pos[r] < 0 are skipped (their output is not written). Needs no
+   workspace: the context splits merge inside a thread-block cluster. The
+   cache rows written are bit-identical to accel_b200_rope_append's; the
+   attention output agrees with accel_b200_attention_decode within 1e-4. A
+   bulk copy that does not land within the wait bound ORs
+   ACCEL_B200_STATUS_COPY_TIMEOUT into *status (device int; may be NULL). */
+ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld, const int32_t* row_seq,
+                                               const int32_t* row_pos, int64_t rows, int32_t heads, int32_t kv_heads,
+                                               int32_t head_dim, const float* cos_table, const float* sin_table,
+                                               int32_t context, float* k_cache, float* v_cache, int64_t seq_stride,
+                                               int64_t head_stride, float* out, int64_t out_ld, int32_t* status,
+                                               void* stream);
+
 /* SiluMul (src/sim_silu.cc:8-13) over fused rows [gate (inter) | up (inter)]
    of row stride ld into out[r, i] (row stride ldo). */
 ACCEL_B200_API int accel_b200_silu_mul_rows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows,

@@ -1,0 +1,115 @@
+"""The fused decode step accel_b200_decode_attention (Rope, AppendCache and
+attention for one new token per sequence): the cache rows it writes against
+accel_b200_rope_append bit for bit, and the attention output against the
+CPU checker's Rope + Attention (src/sim_rope.cc, src/sim_attend.cc:9-46)
+within 1e-4, over ragged positions (chunk edges, one row, the full context)
+and finished rows."""
+
+import numpy as np
+import pytest
+import torch
+
+from accelep_b200 import kernels as K
+from accelep_b200._lib import B200Error
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a, dtype=None):
+    t = torch.as_tensor(np.ascontiguousarray(a))
+    return t.to(dtype).to("cuda") if dtype is not None else t.to("cuda")
+
+
+def H(t):
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+def close(got, want):
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+def tables(ctx, hd, theta=10000.0):
+    inv = 1.0 / theta ** (np.arange(0, hd, 2, dtype=np.float64) / hd)
+    ang = np.outer(np.arange(ctx, dtype=np.float64), inv)
+    ang = np.concatenate([ang, ang], axis=1)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+@pytest.mark.parametrize("heads,kvh,ctx,pos", [
+    (9, 3, 1300, [0, 63, 64, 700, 1299, -1, 127, 1000]),
+    (4, 4, 200, [5, 199, -1, 64]),
+    (8, 1, 520, [511, 512, 0]),
+])
+def test_decode_attention_matches(lib, cuda, orc, heads, kvh, ctx, pos):
+    hd = 64
+    rng = np.random.default_rng(ctx + heads)
+    rows = len(pos)
+    pos = np.array(pos, np.int32)
+    seq = np.arange(rows, dtype=np.int32)[::-1].copy()  # slots in another order than rows
+    qkv = rng.standard_normal((rows, (heads + 2 * kvh) * hd), dtype=np.float32)
+    kc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    vc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    cos_t, sin_t = tables(ctx, hd)
+    cos_d, sin_d = T(cos_t), T(sin_t)
+
+    # Fused step.
+    kc_f, vc_f, qkv_f = T(kc), T(vc), T(qkv)
+    out = torch.full((rows, heads * hd), 7.0, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.decode_attention(qkv_f, T(pos), heads, kvh, cos_d, sin_d, kc_f, vc_f, row_seq=T(seq), out=out, status=status)
+    got = H(out)
+    assert H(status)[0] == 0
+    assert np.array_equal(H(qkv_f), qkv)  # the input rows are only read
+
+    # Separate Rope + AppendCache: the same cache bits.
+    kc_r, vc_r, qkv_r = T(kc), T(vc), T(qkv)
+    K.rope_append(qkv_r, T(seq), T(pos), heads, kvh, hd, cos_d, sin_d, kc_r, vc_r)
+    assert np.array_equal(H(kc_f), H(kc_r))
+    assert np.array_equal(H(vc_f), H(vc_r))
+
+    kc_after = H(kc_r)
+    vc_after = H(vc_r)
+    for r in range(rows):
+        if pos[r] < 0:
+            assert (got[r] == 7.0).all()  # finished: not written
+            continue
+        p, s = int(pos[r]), int(seq[r])
+        q = orc.rope(qkv[r, :heads * hd].copy(), cos_t, sin_t, 1, heads, hd, p)
+        k_ref = np.ascontiguousarray(kc_after[s, :, :p + 1].transpose(1, 0, 2))  # [t, kv head, d]
+        v_ref = np.ascontiguousarray(vc_after[s, :, :p + 1].transpose(1, 0, 2))
+        want = orc.attend(q.reshape(1, heads, hd), k_ref, v_ref, 1, p, heads, kvh, hd)
+        close(got[r], want.reshape(-1))
+
+
+def test_decode_attention_every_split_boundary(lib, cuda, orc):
+    """Every length from 1 to 300 in one batch: all chunk and split edges."""
+    heads, kvh, hd, ctx = 6, 2, 64, 300
+    rng = np.random.default_rng(9)
+    pos = np.arange(ctx, dtype=np.int32)
+    rows = len(pos)
+    qkv = rng.standard_normal((rows, (heads + 2 * kvh) * hd), dtype=np.float32)
+    kc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    vc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    cos_t, sin_t = tables(ctx, hd)
+    kc_f, vc_f = T(kc), T(vc)
+    got = H(K.decode_attention(T(qkv), T(pos), heads, kvh, T(cos_t), T(sin_t), kc_f, vc_f))
+    kc_after, vc_after = H(kc_f), H(vc_f)
+    for r in range(0, rows, 7):
+        p = int(pos[r])
+        q = orc.rope(qkv[r, :heads * hd].copy(), cos_t, sin_t, 1, heads, hd, p)
+        k_ref = np.ascontiguousarray(kc_after[r, :, :p + 1].transpose(1, 0, 2))
+        v_ref = np.ascontiguousarray(vc_after[r, :, :p + 1].transpose(1, 0, 2))
+        want = orc.attend(q.reshape(1, heads, hd), k_ref, v_ref, 1, p, heads, kvh, hd)
+        close(got[r], want.reshape(-1))
+
+
+def test_decode_attention_rejects(lib, cuda):
+    q = torch.zeros(2, 9 * 64 + 6 * 64, device="cuda")
+    kc = torch.zeros(2, 3, 16, 64, device="cuda")
+    pos = torch.zeros(2, dtype=torch.int32, device="cuda")
+    cs = torch.zeros(16, 64, device="cuda")
+    with pytest.raises(B200Error):
+        K.decode_attention(q, pos, 9, 4, cs, cs, kc, kc)  # 9 heads over 4 kv heads
+    with pytest.raises(B200Error):
+        K.decode_attention(torch.zeros(2, 100, device="cuda"), pos, 9, 3, cs, cs, kc, kc)  # row stride too small
