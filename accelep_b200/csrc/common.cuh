@@ -6,6 +6,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 
 #include "accel_b200.h"
 #include "status.h"
@@ -30,7 +31,47 @@ constexpr int64_t kMaxCounters = static_cast<int64_t>(kCounterRegion / sizeof(in
 __host__ __device__ __forceinline__ int64_t Min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t Max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
+// Programmatic dependent launch: kernels launched through LaunchK may start
+// while the previous kernel on the stream is still running. Each such kernel
+// calls PdlWait before it touches memory that an earlier kernel writes (and
+// before any global write of its own); only immutable inputs (weights,
+// scales, tables) are read before it. PdlTrigger lets the next kernel start.
+// Off when the environment sets ACCEL_B200_PDL=0.
+bool PdlEnabled();
+
+// Launches `kernel` with an optional thread-block cluster (cx, cy, 1) and, when
+// enabled, programmatic stream serialization.
+template <typename... KArgs, typename... Args>
+cudaError_t LaunchK(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, unsigned cx,
+                    unsigned cy, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (cx * cy > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cx;
+    attr[n].val.clusterDim.y = cy;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (PdlEnabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // ---------------------------------------------------------------- device side
+
+__device__ __forceinline__ void PdlWait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void PdlTrigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float WarpSum(float v) {
 #pragma unroll

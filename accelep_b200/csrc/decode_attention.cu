@@ -75,6 +75,8 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   __shared__ __align__(16) float mo[G * kD];  // published weighted values
   __shared__ float m_run[G], l_run[G], corr[G];
   __shared__ int32_t ok_s;
+  PdlTrigger();
+  PdlWait();  // row positions, q|k|v rows and the cache come from earlier kernels
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = static_cast<int>(blockIdx.x), S = static_cast<int>(gridDim.x);
   const int g = static_cast<int>(blockIdx.y);
@@ -290,24 +292,10 @@ int LaunchFused(const FusedArgs& a, int64_t rows, cudaStream_t stream) {
     cudaFuncSetAttribute(AttnDecodeFusedKernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
   const int S = SplitFor(rows, a.kv_heads, a.context);
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(S), static_cast<unsigned>(a.kv_heads), static_cast<unsigned>(rows));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, AttnDecodeFusedKernel<G>, a);
-  if (err != cudaSuccess) {
-    cudaGetLastError();
-    return SetError(ACCEL_B200_ECUDA, std::string("decode_attention: ") + cudaGetErrorString(err));
-  }
-  return CheckLaunch("decode_attention");
+  const dim3 grid(static_cast<unsigned>(S), static_cast<unsigned>(a.kv_heads), static_cast<unsigned>(rows));
+  return CheckLaunchEx(LaunchK(AttnDecodeFusedKernel<G>, grid, dim3(kThreads), kSmemBytes, stream,
+                               static_cast<unsigned>(S), 1u, a),
+                       "decode_attention");
 }
 
 }  // namespace

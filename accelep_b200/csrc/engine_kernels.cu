@@ -65,6 +65,8 @@ __global__ void RopeAppendKernel(float* __restrict__ qkv, int64_t ld, const int3
 
 __global__ void SiluMulRowsKernel(const float* __restrict__ gu, int64_t ld, float* __restrict__ out, int64_t ldo,
                                   int64_t rows, int64_t inter) {
+  PdlTrigger();
+  PdlWait();
   const int64_t total = rows * inter;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -103,6 +105,8 @@ __global__ void GreedyStepKernel(const float* __restrict__ logits, const int32_t
                                  int32_t batch) {
   __shared__ Best red[32];
   __shared__ int32_t last;
+  PdlTrigger();
+  PdlWait();
   const int b = blockIdx.x;
   const int32_t n = *step;
   const bool live = done[b] == 0;
@@ -178,6 +182,17 @@ __global__ void GatherRowsKernel(const float* __restrict__ src, int64_t ld, cons
 }
 
 }  // namespace
+
+int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
+                      cudaStream_t stream) {
+  if (rows < 0 || inter < 0 || ld < 2 * inter || ldo < inter) return SetError(ACCEL_B200_EINVAL, "silu_mul_rows: bad arguments");
+  if (rows * inter == 0) return ClearError();
+  const int64_t blocks = CeilDiv(rows * inter, 256);
+  const int grid = static_cast<int>(blocks < kSms * 8 ? blocks : kSms * 8);
+  return CheckLaunchEx(LaunchK(SiluMulRowsKernel, dim3(grid), dim3(256), 0, stream, 1u, 1u, gate_up, ld, out, ldo, rows,
+                               inter),
+                       "silu_mul_rows");
+}
 }  // namespace accel_b200
 
 using namespace accel_b200;
@@ -203,12 +218,7 @@ ACCEL_B200_API int accel_b200_rope_append(float* qkv, int64_t qkv_ld, const int3
 
 ACCEL_B200_API int accel_b200_silu_mul_rows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows,
                                             int64_t inter, void* stream) {
-  if (rows < 0 || inter < 0 || ld < 2 * inter || ldo < inter) return SetError(ACCEL_B200_EINVAL, "silu_mul_rows: bad arguments");
-  if (rows * inter == 0) return ClearError();
-  const int64_t blocks = CeilDiv(rows * inter, 256);
-  const int grid = static_cast<int>(blocks < kSms * 8 ? blocks : kSms * 8);
-  SiluMulRowsKernel<<<grid, 256, 0, AsStream(stream)>>>(gate_up, ld, out, ldo, rows, inter);
-  return CheckLaunch("silu_mul_rows");
+  return LaunchSiluMulRows(gate_up, ld, out, ldo, rows, inter, AsStream(stream));
 }
 
 ACCEL_B200_API int accel_b200_greedy_step(const float* logits, const int32_t* pre_ids, int64_t vocab, int64_t ld,
@@ -217,9 +227,10 @@ ACCEL_B200_API int accel_b200_greedy_step(const float* logits, const int32_t* pr
                                           int32_t* row_pos, int32_t* lens, int32_t eos, int32_t context,
                                           int32_t* step, int32_t* finished, int32_t batch, void* stream) {
   if (batch <= 0 || vocab <= 0 || ld < vocab || step == nullptr) return SetError(ACCEL_B200_EINVAL, "greedy_step: bad arguments");
-  GreedyStepKernel<<<batch, 1024, 0, AsStream(stream)>>>(logits, pre_ids, vocab, ld, ids, ids_stride, count, done, tokens,
-                                                         row_pos, lens, eos, context, step, finished, batch);
-  return CheckLaunch("greedy_step");
+  return CheckLaunchEx(LaunchK(GreedyStepKernel, dim3(batch), dim3(1024), 0, AsStream(stream), 1u, 1u, logits, pre_ids,
+                               vocab, ld, ids, ids_stride, count, done, tokens, row_pos, lens, eos, context, step,
+                               finished, batch),
+                       "greedy_step");
 }
 
 ACCEL_B200_API int accel_b200_gather_rows(const float* src, int64_t ld, const int32_t* idx, int64_t rows, int64_t cols,

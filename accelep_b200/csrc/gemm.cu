@@ -341,9 +341,11 @@ int EmptySum(float* c, int64_t ldc, int64_t m, int64_t n, const Epilogue& ep, cu
 bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
                 int64_t n);
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n);
-int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c, int64_t ldc,
-          int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace, size_t workspace_bytes,
-          int32_t* status, cudaStream_t stream);
+int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale,
+          float* c, int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace,
+          size_t workspace_bytes, int32_t* status, cudaStream_t stream);
+int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
+                      cudaStream_t stream);
 
 namespace {
 std::atomic<int> g_q8_path{0};  // 0: by shape, 1: CUDA cores, 2: tensor cores where eligible
@@ -404,8 +406,8 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
   }
   const int8_t* w = b->q + b->offset;
   if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
-    return RunTc(a, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace, workspace_bytes, nullptr,
-                 AsStream(stream));
+    return RunTc(a, nullptr, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace, workspace_bytes,
+                 nullptr, AsStream(stream));
   }
   g.a = a;
   g.lda = lda;
@@ -419,6 +421,46 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
   g.k = k;
   g.n = n;
   return RunGemm<int8_t>(g, AsStream(stream), workspace, workspace_bytes);
+}
+
+ACCEL_B200_API size_t accel_b200_matmul_q8_silu_workspace(int64_t m, int64_t inter, int64_t n) {
+  // The product's workspace, then room for the SiluMul rows when the product
+  // runs on the CUDA cores (which read A from memory).
+  const size_t base = (accel_b200_matmul_q8_workspace(m, inter, n) + 255) / 256 * 256;
+  return base + static_cast<size_t>(m > 0 ? m : 0) * static_cast<size_t>(inter > 0 ? inter : 0) * sizeof(float);
+}
+
+ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, int64_t inter,
+                                             const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
+                                             int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+  if (m < 0 || inter < 0 || n < 0 || b == nullptr || ld < 2 * inter) {
+    return SetError(ACCEL_B200_EINVAL, "quantized MatMul (SiluMul rows) is out of range");
+  }
+  if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
+  Epilogue e{};
+  if (!ToEpilogue(ep, &e)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
+  if (m == 0 || n == 0) return ClearError();
+  if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
+  if (inter == 0) return EmptySum(c, ldc, m, n, e, AsStream(stream));
+  if (gate_up == nullptr || b->q == nullptr || b->scale == nullptr) {
+    return SetError(ACCEL_B200_EINVAL, "quantized MatMul is missing an operand");
+  }
+  const size_t need = accel_b200_matmul_q8_silu_workspace(m, inter, n);
+  if (workspace == nullptr || workspace_bytes < need) return SetError(ACCEL_B200_EINVAL, "matmul_q8_silu: workspace too small");
+  const int8_t* w = b->q + b->offset;
+  const float* up = gate_up + inter;
+  if (inter % 4 == 0 && UseTc(gate_up, ld, w, b->axis, b->zero, m, inter, n) &&
+      reinterpret_cast<uintptr_t>(up) % 16 == 0) {
+    return RunTc(gate_up, up, ld, w, b->scale, b->axis < 0, c, ldc, m, inter, n, e, workspace, workspace_bytes,
+                 nullptr, AsStream(stream));
+  }
+  // CUDA cores: SiluMul rows into the workspace's tail, then the product.
+  const size_t base = need - static_cast<size_t>(m) * inter * sizeof(float);
+  float* act = reinterpret_cast<float*>(static_cast<char*>(workspace) + base);
+  const int rc = LaunchSiluMulRows(gate_up, ld, act, inter, m, inter, AsStream(stream));
+  if (rc != ACCEL_B200_OK) return rc;
+  return accel_b200_matmul_q8(act, inter, b, c, ldc, m, inter, n, ep, workspace, base, stream);
 }
 
 ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const float* b, float* c, int64_t ldc, int64_t m,

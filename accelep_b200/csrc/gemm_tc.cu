@@ -3,33 +3,47 @@
 // C[m, n] = epilogue(scale[n] * sum_k A[m, k] * q[k, n]) with A fp32 [m, k], q int8
 // [k, n] (n contiguous: the reference's QuantPlane layout) and a per-column
 // (or single) scale: src/sim_device.cc:541-602 and the epilogue of
-// src/runtime.cc:332-344.
+// src/runtime.cc:332-344. A may also be SiluMul of a fused gate|up row
+// (src/sim_silu.cc:8-13 then the down projection, src/llama_model.cc:239-240).
 //
 // Arithmetic. int8 -> bf16 is exact (|q| <= 128 needs 8 significant bits).
-// Each fp32 activation is split once into three bf16 planes hi + mid + lo
-// (each the rounded remainder of the previous); together they carry the
-// 24-bit fp32 significand, every product with the bf16 weight is exact, and
-// three MMAs per k step accumulate in fp32 in TMEM. The MMA is issued
-// "swapped": M = 128 runs over output features and N = R over activation rows,
-// so decode with 32 rows is a full-width MMA.
+// Each fp32 activation is split into three bf16 planes hi + mid + lo (each the
+// rounded remainder of the previous); together they carry the 24-bit fp32
+// significand, every product with the bf16 weight is exact, and the planes
+// accumulate separately in fp32 in TMEM. The MMA is issued "swapped": M = 128
+// runs over output features and N over activation rows (all three planes in
+// one MMA of N = 3R when 3R <= 256), so decode with 32 rows is a full-width MMA.
+//
+// Activation operand, by mode:
+//   planes  (m > 64): a separate pass writes the three planes [3][m][k] to the
+//           workspace; TMA loads them with 128-byte swizzle, which is already
+//           the MMA's K-major canonical layout.
+//   fp32    (m <= 64): TMA loads the fp32 tile [R rows x 64 k]; the converter
+//           warps split it into the planes in shared memory.
+//   silu    (m <= 64): TMA loads the gate and up tiles; the converter warps form
+//           silu(g) * u exactly as SiluMul rounds it and split the result.
 //
 // Pipeline (one CTA = one 128-feature x R-row tile over a range of 64-deep k
 // blocks; 6 warps):
-//   warp 0  producer: per k block, one TMA of the raw int8 weight block
-//           [64 k x 128 n] and one TMA of the three activation planes
-//           [3 x R x 64 k] with 128-byte swizzle, which is already the MMA's
-//           K-major canonical layout; a ring of raw stages.
+//   warp 0  producer: per k block one TMA of the raw int8 weight block
+//           [64 k x 128 n] and the activation load(s) of the mode; a ring of
+//           stages.
 //   warps 2-5 converters: int8 -> bf16 (integer and fp32-add bit arithmetic,
-//           exact) into the MMA's n-contiguous swizzled layout (two buffers);
-//           afterwards the epilogue: tcgen05.ld of the accumulator into a
-//           shared tile, then scale, fused epilogue and coalesced row stores.
-//   warp 1  MMA issuer (one thread): 3 planes x 4 k steps per block, then
-//           tcgen05.commit to the barriers that free the stage and buffer.
+//           exact) into the MMA's n-contiguous swizzled layout (two buffers),
+//           and the split of fp32 activations; afterwards the epilogue:
+//           tcgen05.ld of the accumulator into a shared tile, then scale,
+//           fused epilogue and coalesced row stores.
+//   warp 1  MMA issuer (one thread): 4 k steps per block, then tcgen05.commit
+//           to the barriers that free the stage and the buffer.
 // K can be split across the CTAs of one thread-block cluster (up to 8); each
 // keeps its partial tile in shared memory and the cluster sums the tiles in
 // rank order through distributed shared memory, so the result is
-// deterministic and no partial sums go to global memory. Every mbarrier wait
-// is bounded (tma.cuh).
+// deterministic and no partial sums go to global memory.
+//
+// Launch overlap: the kernel is launched with programmatic stream
+// serialization. Before griddepcontrol.wait it only sets up barriers and TMEM
+// and loads weights (immutable); activations, residuals and the output are
+// touched after it. Every mbarrier wait is bounded (tma.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -59,15 +73,21 @@ constexpr int kConvWarps = 4;
 constexpr int kThreads = (2 + kConvWarps) * 32;
 constexpr int kMaxStages = 4;
 
-template <int R, int S>
+enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2 };
+
+template <int R, int S, int M>
 struct Tc {
-  static constexpr int kXBytes = 3 * R * kBk * 2;    // three bf16 planes
-  static constexpr int kStage = kXBytes + kWRaw;     // planes first: 1024-aligned
+  static constexpr int kXBytes = 3 * R * kBk * 2;  // three bf16 planes (MMA operand)
+  static constexpr int kXRaw = M == kAPlanes ? 0 : (M == kASilu ? 2 : 1) * R * kBk * 4;  // fp32 tiles
+  static constexpr int kXLoad = M == kAPlanes ? kXBytes : kXRaw;  // bytes the activation TMA delivers
+  static constexpr int kStage = kXBytes + kWRaw + kXRaw;          // planes first: 1024-aligned
   static constexpr int kStages = S;
-  static constexpr int kTile = R * kBn * 4;          // fp32 accumulator tile, staged in stage memory
+  static constexpr int kTile = R * kBn * 4;  // fp32 accumulator tile, staged in stage memory
   static constexpr int kStageArea = kStages * kStage > kTile ? kStages * kStage : kTile;
   static constexpr int kSmem = kStageArea + kConvBufs * kWConv + 1024;
   static_assert(kStages <= kMaxStages, "stage count");
+  static_assert(kStage % 1024 == 0, "stage alignment");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct TcArgs {
@@ -144,10 +164,61 @@ __device__ __forceinline__ void ConvertWeightBlock(const uint8_t* raw, uint8_t* 
   }
 }
 
-template <int R, int kStagesT>
+// hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid).
+__device__ __forceinline__ void Split3(float x, float* hi, float* mid, float* lo) {
+  *hi = __bfloat162float(__float2bfloat16_rn(x));
+  const float r1 = x - *hi;
+  *mid = __bfloat162float(__float2bfloat16_rn(r1));
+  *lo = r1 - *mid;
+}
+
+// SiluMul of one element as src/sim_silu.cc:8-13 rounds it.
+__device__ __forceinline__ float SiluMul(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+}
+
+// fp32 activation tile(s) [R rows][64 k] (rows of 256 bytes) -> the three bf16
+// planes in the K-major 128-byte-swizzled layout the planes TMA would write:
+// plane p, row r at p * R * 128 + r * 128, 16-byte chunk j stored at
+// j ^ (r % 8). Each thread takes four consecutive k of one row per pass.
+// Rows at or past `valid` are skipped: their planes stay zero.
+template <int R, int M>
+__device__ __forceinline__ void SplitTile(const uint8_t* raw, uint8_t* planes, int ct, int valid) {
+#pragma unroll
+  for (int pass = 0; pass < R * 16 / (kConvWarps * 32); ++pass) {
+    const int idx = pass * (kConvWarps * 32) + ct;
+    const int row = idx >> 4, k4 = idx & 15;
+    if (pass * (kConvWarps * 32) >= valid * 16) break;  // uniform across the CTA
+    if (row >= valid) continue;
+    float x[4];
+    const float4 v = *reinterpret_cast<const float4*>(raw + row * 256 + k4 * 16);
+    if constexpr (M == kASilu) {
+      const float4 u = *reinterpret_cast<const float4*>(raw + R * 256 + row * 256 + k4 * 16);
+      x[0] = SiluMul(v.x, u.x);
+      x[1] = SiluMul(v.y, u.y);
+      x[2] = SiluMul(v.z, u.z);
+      x[3] = SiluMul(v.w, u.w);
+    } else {
+      x[0] = v.x;
+      x[1] = v.y;
+      x[2] = v.z;
+      x[3] = v.w;
+    }
+    float h[4], md[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) Split3(x[j], &h[j], &md[j], &lo[j]);
+    const int off = row * 128 + (((k4 >> 1) ^ (row & 7)) << 4) + (k4 & 1) * 8;
+    *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(h[0], h[1]), PackBf16(h[2], h[3]));
+    *reinterpret_cast<uint2*>(planes + R * 128 + off) = make_uint2(PackBf16(md[0], md[1]), PackBf16(md[2], md[3]));
+    *reinterpret_cast<uint2*>(planes + 2 * R * 128 + off) = make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+  }
+}
+
+template <int R, int kStagesT, int M>
 __global__ void __launch_bounds__(kThreads, 1)
-    Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, TcArgs g) {
-  using L = Tc<R, kStagesT>;
+    Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+                   const __grid_constant__ CUtensorMap tu, TcArgs g) {
+  using L = Tc<R, kStagesT, M>;
   constexpr int S = L::kStages;
   // The three activation planes are 3R consecutive K-major rows in shared
   // memory: one MMA with N = 3R covers all of them when 3R <= 256 and reads the
@@ -156,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kCols = 3 * R <= 128 ? 128 : (3 * R <= 256 ? 256 : 512);
   constexpr uint32_t kIdesc = InstrDescBf16(kOneMma ? 3 * R : R, true);
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], cfull[kConvBufs], cempty[kConvBufs], accf;
+  __shared__ __align__(8) uint64_t full_w[kMaxStages], full_x[kMaxStages], empty[kMaxStages], cfull[kConvBufs],
+      cempty[kConvBufs], accf;
   __shared__ uint32_t tmem_s;
   __shared__ int32_t ok_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -168,10 +240,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb_begin = blockIdx.y * g.kb_per_split;
   const int nkb = max(0, min(g.kb_total, kb_begin + g.kb_per_split) - kb_begin);
 
+  PdlTrigger();
   if (warp == 1) TmemAlloc(&tmem_s, kCols);
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      MbarInit(&full[s], 1);
+      MbarInit(&full_w[s], 1);
+      MbarInit(&full_x[s], 1);
       MbarInit(&empty[s], 1 + kConvWarps);
     }
     for (int c = 0; c < kConvBufs; ++c) {
@@ -191,21 +265,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+      // Weights of the first stages before the wait: they are immutable.
+      const int pre = min(S, nkb);
+      for (int i = 0; i < pre; ++i) {
+        MbarArriveExpectTx(&full_w[i], kWRaw);
+        TmaLoad2D(smem + i * L::kStage + L::kXBytes, &tw, static_cast<int32_t>(n0), (kb_begin + i) * kBk, &full_w[i]);
+      }
+      PdlWait();
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
-        ok &= MbarWait(&empty[s], ((i / S) & 1) ^ 1);
         uint8_t* stage = smem + s * L::kStage;
         const int32_t k0 = (kb_begin + i) * kBk;
-        MbarArriveExpectTx(&full[s], L::kStage);
-        TmaLoad3D(stage, &tx, k0, static_cast<int32_t>(row0), 0, &full[s]);
-        TmaLoad2D(stage + L::kXBytes, &tw, static_cast<int32_t>(n0), k0, &full[s]);
+        if (i >= S) {
+          ok &= MbarWait(&empty[s], ((i / S) & 1) ^ 1);
+          MbarArriveExpectTx(&full_w[s], kWRaw);
+          TmaLoad2D(stage + L::kXBytes, &tw, static_cast<int32_t>(n0), k0, &full_w[s]);
+        }
+        MbarArriveExpectTx(&full_x[s], L::kXLoad);
+        if constexpr (M == kAPlanes) {
+          TmaLoad3D(stage, &tx, k0, static_cast<int32_t>(row0), 0, &full_x[s]);
+        } else {
+          uint8_t* xraw = stage + L::kXBytes + kWRaw;
+          TmaLoad2D(xraw, &tx, k0, static_cast<int32_t>(row0), &full_x[s]);
+          if constexpr (M == kASilu) TmaLoad2D(xraw + R * 256, &tu, k0, static_cast<int32_t>(row0), &full_x[s]);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S, c = i % kConvBufs;
-        ok &= MbarWait(&full[s], (i / S) & 1);
+        if constexpr (M == kAPlanes) ok &= MbarWait(&full_x[s], (i / S) & 1);
         ok &= MbarWait(&cfull[c], (i / kConvBufs) & 1);
         TcFenceAfterSync();
         const uint32_t a_addr = SmemAddr(conv_base + c * kWConv);
@@ -234,11 +324,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int ct = tid - 64;
+    const int valid = static_cast<int>(Min64(R, g.m - row0));
+    if constexpr (M != kAPlanes) {
+      // Rows past the matrix: zero planes in every stage, written once.
+      if (valid < R) {
+        for (int s = 0; s < S; ++s) {
+          uint8_t* planes = smem + s * L::kStage;
+          for (int idx = ct; idx < 3 * (R - valid) * 8; idx += kConvWarps * 32) {
+            const int p = idx / ((R - valid) * 8), rem = idx % ((R - valid) * 8);
+            *reinterpret_cast<uint4*>(planes + p * R * 128 + (valid + rem / 8) * 128 + (rem % 8) * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+    }
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S, c = i % kConvBufs;
-      ok &= MbarWait(&full[s], (i / S) & 1);
+      uint8_t* stage = smem + s * L::kStage;
+      ok &= MbarWait(&full_w[s], (i / S) & 1);
       ok &= MbarWait(&cempty[c], ((i / kConvBufs) & 1) ^ 1);
-      ConvertWeightBlock(smem + s * L::kStage + L::kXBytes, conv_base + c * kWConv, ct);
+      ConvertWeightBlock(stage + L::kXBytes, conv_base + c * kWConv, ct);
+      if constexpr (M != kAPlanes) {
+        ok &= MbarWait(&full_x[s], (i / S) & 1);
+        SplitTile<R, M>(stage + L::kXBytes + kWRaw, stage, ct, valid);
+      }
       FenceProxyAsyncSmem();
       __syncwarp();
       if (lane == 0) {
@@ -248,6 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (nkb > 0) ok &= MbarWait(&accf, 0);
   }
+  // Every thread past this point may read the residual or write the output.
+  PdlWait();
   const bool cta_ok = __syncthreads_and(ok);
   if (!cta_ok) {
     // A wait ran out: report it and let the tensor core finish (bounded). The
@@ -349,10 +460,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   ClusterSync();  // no CTA leaves while a peer may still read its tile
 }
 
-// fp32 [m, k] (row stride lda) -> three bf16 planes [3][m][k]: hi = bf16(x),
-// mid = bf16(x - hi), lo = bf16(x - hi - mid).
-__global__ void SplitPlanesKernel(const float* __restrict__ a, int64_t lda, int64_t m, int64_t k,
-                                  __nv_bfloat16* __restrict__ planes) {
+// fp32 [m, k] (row stride lda) -> three bf16 planes [3][m][k] (Split3). With
+// `up` set, the element is SiluMul(a[r][i], up[r][i]) first.
+__global__ void SplitPlanesKernel(const float* __restrict__ a, const float* __restrict__ up, int64_t lda, int64_t m,
+                                  int64_t k, __nv_bfloat16* __restrict__ planes) {
+  PdlTrigger();
+  PdlWait();
   const int64_t quads = k / 4;
   const int64_t total = m * quads;
   const int64_t plane = m * k;
@@ -360,15 +473,17 @@ __global__ void SplitPlanesKernel(const float* __restrict__ a, int64_t lda, int6
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = idx / quads, q = idx - r * quads;
     const float4 v = __ldg(reinterpret_cast<const float4*>(a + r * lda + q * 4));
-    const float x[4] = {v.x, v.y, v.z, v.w};
+    float x[4] = {v.x, v.y, v.z, v.w};
+    if (up != nullptr) {
+      const float4 u = __ldg(reinterpret_cast<const float4*>(up + r * lda + q * 4));
+      x[0] = SiluMul(x[0], u.x);
+      x[1] = SiluMul(x[1], u.y);
+      x[2] = SiluMul(x[2], u.z);
+      x[3] = SiluMul(x[3], u.w);
+    }
     float hi[4], mid[4], lo[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      hi[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
-      const float r1 = x[i] - hi[i];
-      mid[i] = __bfloat162float(__float2bfloat16_rn(r1));
-      lo[i] = r1 - mid[i];
-    }
+    for (int i = 0; i < 4; ++i) Split3(x[i], &hi[i], &mid[i], &lo[i]);
     const int64_t off = r * k + q * 4;
     *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(hi[0], hi[1]), PackBf16(hi[2], hi[3]));
     *reinterpret_cast<uint2*>(planes + plane + off) = make_uint2(PackBf16(mid[0], mid[1]), PackBf16(mid[2], mid[3]));
@@ -378,13 +493,21 @@ __global__ void SplitPlanesKernel(const float* __restrict__ a, int64_t lda, int6
 
 struct TcPlan {
   int r;
+  int mode;  // AMode
   int stages;
   int64_t feature_tiles, row_tiles;
   int32_t kb_total, kb_per_split, splits;
   size_t planes_bytes;
 };
 
-TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n) {
+// Stages that fit the shared memory of one CTA (at most 4).
+template <int R, int M>
+constexpr int MaxStages() {
+  constexpr int stage = 3 * R * kBk * 2 + kWRaw + (M == kAPlanes ? 0 : (M == kASilu ? 2 : 1) * R * kBk * 4);
+  return stage * 4 + kConvBufs * kWConv + 1024 <= 227 * 1024 ? 4 : 3;
+}
+
+TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu) {
   TcPlan p{};
   p.r = m <= 32 ? 32 : (m <= 64 ? 64 : 128);
   p.feature_tiles = CeilDiv(n, kBn);
@@ -401,8 +524,12 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n) {
   }
   p.kb_per_split = static_cast<int32_t>(CeilDiv(p.kb_total, splits));
   p.splits = static_cast<int32_t>(CeilDiv(p.kb_total, p.kb_per_split));
-  p.stages = p.kb_per_split <= 2 ? 2 : (p.r <= 64 ? 4 : 3);
-  p.planes_bytes = (static_cast<size_t>(3) * m * k * 2 + 1023) / 1024 * 1024;
+  p.stages = p.kb_per_split <= 2 ? 2 : 4;  // 4: as many as fit (MaxStages)
+  // Splitting fp32 tiles in the kernel saves the planes pass (one launch) but
+  // adds converter work to every k block: worth it for CTAs that walk few
+  // blocks (latency-bound decode products), not for long weight streams.
+  p.mode = p.r == 128 || p.kb_per_split > 4 ? kAPlanes : (silu ? kASilu : kAF32);
+  p.planes_bytes = p.mode == kAPlanes ? (static_cast<size_t>(3) * m * k * 2 + 1023) / 1024 * 1024 : 0;
   return p;
 }
 
@@ -420,43 +547,38 @@ PFN_cuTensorMapEncodeTiled_v12000 EncodeFn() {
   return fn;
 }
 
-template <int R, int ST>
-int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
+template <int R, int ST, int M>
+int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g, const TcPlan& p,
+             cudaStream_t s) {
+  using L = Tc<R, ST, M>;
   static std::once_flag once[16];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 15], [] {
-    cudaFuncSetAttribute(Q8GemmTcKernel<R, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tc<R, ST>::kSmem);
+    cudaFuncSetAttribute(Q8GemmTcKernel<R, ST, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem);
   });
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
-                     static_cast<unsigned>(p.row_tiles));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Tc<R, ST>::kSmem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = static_cast<unsigned>(p.splits);
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, Q8GemmTcKernel<R, ST>, tw, tx, g);
-  if (err != cudaSuccess) {
-    cudaGetLastError();
-    return SetError(ACCEL_B200_ECUDA, std::string("matmul_q8_tc: ") + cudaGetErrorString(err));
-  }
-  return CheckLaunch("matmul_q8_tc");
+  const dim3 grid(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
+                  static_cast<unsigned>(p.row_tiles));
+  return CheckLaunchEx(LaunchK(Q8GemmTcKernel<R, ST, M>, grid, dim3(kThreads), L::kSmem, s, 1u,
+                               static_cast<unsigned>(p.splits), tw, tx, tu, g),
+                       "matmul_q8_tc");
 }
 
-template <int R>
-int LaunchTcStages(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
-  if (p.stages == 2) return LaunchTc<R, 2>(tw, tx, g, p, s);
-  if constexpr (R <= 64) {
-    return LaunchTc<R, 4>(tw, tx, g, p, s);
-  } else {
-    return LaunchTc<R, 3>(tw, tx, g, p, s);
-  }
+template <int R, int M>
+int LaunchTcStages(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
+                   const TcPlan& p, cudaStream_t s) {
+  if (p.stages == 2) return LaunchTc<R, 2, M>(tw, tx, tu, g, p, s);
+  return LaunchTc<R, MaxStages<R, M>(), M>(tw, tx, tu, g, p, s);
+}
+
+bool Encode2D(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return EncodeFn()(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -474,50 +596,50 @@ bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, cons
 }
 
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
-  const TcPlan p = MakeTcPlan(m, k, n);
+  const TcPlan p = MakeTcPlan(m, k, n, false);
   return kCounterRegion + p.planes_bytes;
 }
 
-int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c, int64_t ldc,
-          int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace, size_t workspace_bytes,
-          int32_t* status, cudaStream_t stream) {
-  const TcPlan p = MakeTcPlan(m, k, n);
-  if (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes) {
+// a: fp32 rows (lda); with `up` set, the product's A is SiluMul(a, up) (same
+// row stride). The caller checked TcEligible for a (and up).
+int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale,
+          float* c, int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace,
+          size_t workspace_bytes, int32_t* status, cudaStream_t stream) {
+  const TcPlan p = MakeTcPlan(m, k, n, up != nullptr);
+  if (p.planes_bytes > 0 && (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes)) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
   }
-  char* ws = static_cast<char*>(workspace);
-  auto* planes = reinterpret_cast<__nv_bfloat16*>(ws + kCounterRegion);
-  {
+  CUtensorMap tw{}, tx{}, tu{};
+  if (!Encode2D(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, n, k, n, kBn, kBk, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8: weight tensor map rejected");
+  }
+  if (p.mode == kAPlanes) {
+    auto* planes = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + kCounterRegion);
     const int64_t total = m * (k / 4);
     const int64_t blocks = CeilDiv(total, 256);
     const int grid = static_cast<int>(blocks < kSms * 16 ? blocks : kSms * 16);
-    SplitPlanesKernel<<<grid, 256, 0, stream>>>(a, lda, m, k, planes);
-    const int rc = CheckLaunch("matmul_q8_split");
+    const int rc = CheckLaunchEx(LaunchK(SplitPlanesKernel, dim3(grid), dim3(256), 0, stream, 1u, 1u, a, up, lda, m,
+                                         k, planes),
+                                 "matmul_q8_split");
     if (rc != ACCEL_B200_OK) return rc;
-  }
-  PFN_cuTensorMapEncodeTiled_v12000 encode = EncodeFn();
-  CUtensorMap tw{}, tx{};
-  {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(k)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(n)};
-    const cuuint32_t box[2] = {kBn, kBk};
-    const cuuint32_t estr[2] = {1, 1};
-    if (encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
-      return SetError(ACCEL_B200_EINVAL, "matmul_q8: weight tensor map rejected");
-    }
-  }
-  {
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m), 3};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) * 2, static_cast<cuuint64_t>(m) * k * 2};
     const cuuint32_t box[3] = {kBk, static_cast<cuuint32_t>(p.r), 3};
     const cuuint32_t estr[3] = {1, 1, 1};
-    if (encode(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, planes, dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    if (EncodeFn()(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, planes, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
       return SetError(ACCEL_B200_EINVAL, "matmul_q8: activation tensor map rejected");
     }
+  } else {
+    // fp32 tiles [R rows x 64 k]; rows and k beyond the matrix read as zero.
+    const uint64_t row_bytes = static_cast<uint64_t>(lda) * 4;
+    if (!Encode2D(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, k, m, row_bytes, kBk, p.r, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        (up != nullptr &&
+         !Encode2D(&tu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, up, k, m, row_bytes, kBk, p.r, CU_TENSOR_MAP_SWIZZLE_NONE))) {
+      return SetError(ACCEL_B200_EINVAL, "matmul_q8: activation tensor map rejected");
+    }
+    if (up == nullptr) tu = tx;
   }
   TcArgs g{};
   g.m = m;
@@ -531,11 +653,19 @@ int RunTc(const float* a, int64_t lda, const int8_t* w, const float* scale, bool
   g.ldc = ldc;
   g.status = status;
   g.ep = ep;
-  switch (p.r) {
-    case 32: return LaunchTcStages<32>(tw, tx, g, p, stream);
-    case 64: return LaunchTcStages<64>(tw, tx, g, p, stream);
-    default: return LaunchTcStages<128>(tw, tx, g, p, stream);
+  if (p.mode == kAPlanes) {
+    switch (p.r) {
+      case 32: return LaunchTcStages<32, kAPlanes>(tw, tx, tu, g, p, stream);
+      case 64: return LaunchTcStages<64, kAPlanes>(tw, tx, tu, g, p, stream);
+      default: return LaunchTcStages<128, kAPlanes>(tw, tx, tu, g, p, stream);
+    }
   }
+  if (p.mode == kASilu) {
+    return p.r == 32 ? LaunchTcStages<32, kASilu>(tw, tx, tu, g, p, stream)
+                     : LaunchTcStages<64, kASilu>(tw, tx, tu, g, p, stream);
+  }
+  return p.r == 32 ? LaunchTcStages<32, kAF32>(tw, tx, tu, g, p, stream)
+                   : LaunchTcStages<64, kAF32>(tw, tx, tu, g, p, stream);
 }
 
 }  // namespace accel_b200

@@ -313,7 +313,7 @@ class Engine {
     CheckIds(ids, count);
     EnsureRows(count, 1);
     PinnedBuf& st = staging;
-    st.Ensure(static_cast<size_t>(count) * 12 + 16);
+    st.Ensure(static_cast<size_t>(count) * 12 + 32);
     int32_t* h = st.as<int32_t>();
     for (int32_t r = 0; r < count; ++r) {
       h[r] = ids[r];
@@ -321,6 +321,13 @@ class Engine {
       h[2 * count + r] = filled + r;
     }
     h[3 * count] = count - 1;
+    h[3 * count + 1] = 0;       // first row of sequence 0
+    h[3 * count + 2] = count;   // its rows
+    h[3 * count + 3] = filled;  // its first position
+    Cuda(cudaMemcpyAsync(seq_first.p, h + 3 * count + 1, 4, cudaMemcpyHostToDevice, stream), "rows");
+    Cuda(cudaMemcpyAsync(seq_count.p, h + 3 * count + 2, 4, cudaMemcpyHostToDevice, stream), "rows");
+    Cuda(cudaMemcpyAsync(seq_pos0.p, h + 3 * count + 3, 4, cudaMemcpyHostToDevice, stream), "rows");
+    prefill_max_rows = count;
     Cuda(cudaMemcpyAsync(tokens.p, h, count * 4, cudaMemcpyHostToDevice, stream), "ids");
     NoteBytesToDevice(static_cast<size_t>(count) * 4);
     Cuda(cudaMemcpyAsync(row_seq.p, h + count, count * 4, cudaMemcpyHostToDevice, stream), "rows");
@@ -354,7 +361,7 @@ class Engine {
     const bool sampled = temperature > 0.f;
 
     PinnedBuf& st = staging;
-    st.Ensure(static_cast<size_t>(rows) * 12 + static_cast<size_t>(batch) * 16 + 64);
+    st.Ensure(static_cast<size_t>(rows) * 12 + static_cast<size_t>(batch) * 28 + 64);
     int32_t* h = st.as<int32_t>();
     int32_t* h_tok = h;
     int32_t* h_seq = h + rows;
@@ -363,8 +370,16 @@ class Engine {
     int32_t* h_lens = h_last + batch;
     uint32_t* h_rng = reinterpret_cast<uint32_t*>(h_lens + batch);
     int32_t* h_ident = reinterpret_cast<int32_t*>(h_rng + batch);
+    int32_t* h_first = h_ident + batch;
+    int32_t* h_count = h_first + batch;
+    int32_t* h_pos0 = h_count + batch;
     int64_t r = 0;
+    prefill_max_rows = 0;
     for (int32_t b = 0; b < batch; ++b) {
+      h_first[b] = static_cast<int32_t>(r);
+      h_count[b] = counts[b];
+      h_pos0[b] = 0;
+      prefill_max_rows = std::max(prefill_max_rows, counts[b]);
       for (int32_t s = 0; s < counts[b]; ++s, ++r) {
         h_tok[r] = prompts[r];
         h_seq[r] = b;
@@ -384,6 +399,9 @@ class Engine {
     Cuda(cudaMemcpyAsync(lens.p, h_lens, batch * 4, cudaMemcpyHostToDevice, stream), "lens");
     Cuda(cudaMemcpyAsync(rng.p, h_rng, batch * 4, cudaMemcpyHostToDevice, stream), "rng");
     Cuda(cudaMemcpyAsync(dec_seq.p, h_ident, batch * 4, cudaMemcpyHostToDevice, stream), "rows");
+    Cuda(cudaMemcpyAsync(seq_first.p, h_first, batch * 4, cudaMemcpyHostToDevice, stream), "rows");
+    Cuda(cudaMemcpyAsync(seq_count.p, h_count, batch * 4, cudaMemcpyHostToDevice, stream), "rows");
+    Cuda(cudaMemcpyAsync(seq_pos0.p, h_pos0, batch * 4, cudaMemcpyHostToDevice, stream), "rows");
     Cuda(cudaMemsetAsync(done.p, 0, batch * 4, stream), "state");
     Cuda(cudaMemsetAsync(count.p, 0, batch * 4, stream), "state");
     Cuda(cudaMemsetAsync(step.p, 0, 16, stream), "state");
@@ -552,6 +570,9 @@ class Engine {
     moved |= normed_last.Ensure(S * H * 4);
     moved |= logits.Ensure(S * cfg.vocab * 4);
     moved |= last_rows.Ensure(S * 4);
+    moved |= seq_first.Ensure(S * 4);
+    moved |= seq_count.Ensure(S * 4);
+    moved |= seq_pos0.Ensure(S * 4);
     moved |= lens.Ensure(S * 4);
     moved |= dec_seq.Ensure(S * 4);
     moved |= dec_pos.Ensure(S * 4);
@@ -565,6 +586,7 @@ class Engine {
     for (int64_t m : {rows, static_cast<int64_t>(seqs)}) {
       for (const Layer& l : layers) {
         for (const Group* g : {&l.qkv, &l.o, &l.gu, &l.down}) ws = std::max(ws, GemmWorkspace(*g, m));
+        if (l.down.kind == WKind::Q8) ws = std::max(ws, accel_b200_matmul_q8_silu_workspace(m, l.down.k, l.down.n));
       }
       ws = std::max(ws, GemmWorkspace(lm_head, std::min<int64_t>(m, seqs)));
     }
@@ -631,15 +653,29 @@ class Engine {
         Abi(accel_b200_rope_append(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
                                    rope_cos.as<float>(), rope_sin.as<float>(), kc, vc, slot_stride, head_stride,
                                    row_stride, stream));
-        Abi(accel_b200_attention_rows(qkv.as<float>(), qkv_ld, kc, vc, row_stride, head_stride, slot_stride,
-                                      mixed.as<float>(), q_out, rseq, decode ? dec_len_pos() : rpos, rows, cfg.heads,
-                                      cfg.kv_heads, head_dim, stream));
+        if (!decode && head_dim == 64 && cfg.heads / cfg.kv_heads <= 4) {
+          Abi(accel_b200_attention_prefill(qkv.as<float>(), qkv_ld, kc, vc, slot_stride, head_stride,
+                                           mixed.as<float>(), q_out, seq_first.as<int32_t>(), seq_count.as<int32_t>(),
+                                           seq_pos0.as<int32_t>(), seqs, prefill_max_rows, cfg.heads, cfg.kv_heads,
+                                           head_dim, stream));
+        } else {
+          Abi(accel_b200_attention_rows(qkv.as<float>(), qkv_ld, kc, vc, row_stride, head_stride, slot_stride,
+                                        mixed.as<float>(), q_out, rseq, decode ? dec_len_pos() : rpos, rows,
+                                        cfg.heads, cfg.kv_heads, head_dim, stream));
+        }
       }
       Gemm(mixed.as<float>(), q_out, l.o, rows, hid, H, &residual);
       Abi(accel_b200_rmsnorm(hid, l.post_norm.as<float>(), normed.as<float>(), rows, H, cfg.eps, 0, stream));
       Gemm(normed.as<float>(), H, l.gu, rows, gu.as<float>(), 2 * I, nullptr);
-      Abi(accel_b200_silu_mul_rows(gu.as<float>(), 2 * I, act.as<float>(), I, rows, I, stream));
-      Gemm(act.as<float>(), I, l.down, rows, hid, H, &residual);
+      if (l.down.kind == WKind::Q8) {
+        // SiluMul feeds the down projection's operand directly.
+        accel_b200_q8_plane plane{l.down.w.as<int8_t>(), l.down.scale.as<float>(), nullptr, 0, 1};
+        Abi(accel_b200_matmul_q8_silu(gu.as<float>(), 2 * I, I, &plane, hid, H, rows, H, &residual, gemm_ws.p,
+                                      gemm_ws.bytes, stream));
+      } else {
+        Abi(accel_b200_silu_mul_rows(gu.as<float>(), 2 * I, act.as<float>(), I, rows, I, stream));
+        Gemm(act.as<float>(), I, l.down, rows, hid, H, &residual);
+      }
     }
     const float* last = hid;
     if (!decode) {
@@ -705,6 +741,9 @@ class Engine {
   int32_t slots = 0;
   DevBuf hidden, normed, qkv, mixed, gu, act, gathered, normed_last, logits;
   DevBuf tokens, row_seq, row_pos, last_rows, lens, dec_seq, dec_pos, done, count, pre_ids, rng, step, finished;
+  // Prefill rows by sequence: first row, row count and first position.
+  DevBuf seq_first, seq_count, seq_pos0;
+  int32_t prefill_max_rows = 0;
   DevBuf ids;
   int32_t ids_rows = 0;
   int64_t ids_stride = 0;

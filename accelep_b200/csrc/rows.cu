@@ -21,6 +21,8 @@ inline int GridFor(int64_t work, int block, int per_sm = 8) {
 // (src/sim_embed.cc:12-15 throws there).
 __global__ void EmbedKernel(const int32_t* __restrict__ ids, int64_t id_offset, const float* __restrict__ table,
                             float* __restrict__ out, int64_t seq, int64_t hidden, int64_t vocab, int32_t* status) {
+  PdlTrigger();
+  PdlWait();
   for (int64_t s = blockIdx.x; s < seq; s += gridDim.x) {
     const int32_t id = ids[id_offset + s];
     if (id < 0 || id >= vocab) {
@@ -44,6 +46,8 @@ __global__ void EmbedKernel(const int32_t* __restrict__ ids, int64_t id_offset, 
 // double reciprocal square root, float(x * inv) * w.
 __global__ void RmsNormKernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
                               int64_t rows, int64_t dim, float eps, int64_t row_offset) {
+  PdlTrigger();
+  PdlWait();
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
@@ -184,9 +188,9 @@ ACCEL_B200_API int accel_b200_embed(const int32_t* ids, int64_t id_offset, const
   if (BadDims(id_offset, seq, hidden, vocab)) return SetError(ACCEL_B200_EINVAL, "embed: negative size");
   if (seq == 0 || hidden == 0) return ClearError();
   if (ids == nullptr || table == nullptr || out == nullptr) return SetError(ACCEL_B200_EINVAL, "embed: null pointer");
-  EmbedKernel<<<GridFor(seq, 1, 16), 128, 0, AsStream(stream)>>>(ids, id_offset, table, out, seq, hidden, vocab,
-                                                                   status);
-  return CheckLaunch("embed");
+  return CheckLaunchEx(LaunchK(EmbedKernel, dim3(GridFor(seq, 1, 16)), dim3(128), 0, AsStream(stream), 1u, 1u, ids,
+                               id_offset, table, out, seq, hidden, vocab, status),
+                       "embed");
 }
 
 ACCEL_B200_API int accel_b200_rmsnorm(const float* x, const float* weight, float* y, int64_t rows, int64_t dim,
@@ -194,8 +198,9 @@ ACCEL_B200_API int accel_b200_rmsnorm(const float* x, const float* weight, float
   if (BadDims(rows, dim, row_offset)) return SetError(ACCEL_B200_EINVAL, "rmsnorm: negative size");
   if (rows == 0 || dim == 0) return ClearError();
   if (x == nullptr || weight == nullptr || y == nullptr) return SetError(ACCEL_B200_EINVAL, "rmsnorm: null pointer");
-  RmsNormKernel<<<GridFor(rows, 8, 16), 256, 0, AsStream(stream)>>>(x, weight, y, rows, dim, eps, row_offset);
-  return CheckLaunch("rmsnorm");
+  return CheckLaunchEx(LaunchK(RmsNormKernel, dim3(GridFor(rows, 8, 16)), dim3(256), 0, AsStream(stream), 1u, 1u, x,
+                               weight, y, rows, dim, eps, row_offset),
+                       "rmsnorm");
 }
 
 ACCEL_B200_API int accel_b200_rope(float* states, const float* cos_table, const float* sin_table, int64_t seq,

@@ -2,6 +2,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "accel_b200.h"
@@ -24,6 +26,24 @@ int ClearError() {
 }
 
 void NoteLaunches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool PdlEnabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ACCEL_B200_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
+
+// Checks a launch made through cudaLaunchKernelEx (its return code) and the
+// error state.
+int CheckLaunchEx(cudaError_t err, const char* what) {
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return SetError(ACCEL_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(err));
+  }
+  return CheckLaunch(what);
+}
 
 int CheckLaunch(const char* what) {
   const cudaError_t err = cudaGetLastError();

@@ -1,6 +1,8 @@
 // Host-side error and launch bookkeeping of the kernel ABI (status.cc).
 #pragma once
 
+#include <cuda_runtime.h>
+
 #include <cstdint>
 #include <string>
 
@@ -13,5 +15,7 @@ int ClearError();
 void NoteLaunches(int64_t n);
 // Checks the launch just issued; returns ACCEL_B200_OK or ACCEL_B200_ECUDA.
 int CheckLaunch(const char* what);
+// The same for a launch whose cudaLaunchKernelEx returned `err`.
+int CheckLaunchEx(cudaError_t err, const char* what);
 
 }  // namespace accel_b200

@@ -40,12 +40,13 @@ __device__ __forceinline__ void MbarArriveExpectTx(uint64_t* bar, uint32_t bytes
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(SmemAddr(bar)), "r"(bytes) : "memory");
 }
 
-// Global -> shared bulk copy completing on `bar`. dst, src and bytes must be
-// multiples of 16.
+// One plain arrival.
 __device__ __forceinline__ void MbarArrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar)) : "memory");
 }
 
+// Global -> shared bulk copy completing on `bar`. dst, src and bytes must be
+// multiples of 16.
 __device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(SmemAddr(dst)),

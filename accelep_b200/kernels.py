@@ -162,6 +162,23 @@ def matmul_q8(a, q, scale, zero=None, axis=1, epilogue=None, out=None, offset=0,
     return c
 
 
+def matmul_q8_silu(gate_up, q, scale, axis=1, epilogue=None, out=None, workspace=None):
+    """SiluMul(gate_up[:, :inter], gate_up[:, inter:]) @ dequant(q); q holds a
+    [inter, n] plane."""
+    lib = load()
+    m, two_inter = gate_up.shape
+    inter = two_inter // 2
+    n = q.shape[-1]
+    c = out if out is not None else torch.zeros(m, n, dtype=torch.float32, device=gate_up.device)
+    plane = Q8Plane(q.data_ptr(), scale.data_ptr(), 0, 0, axis)
+    need = lib.accel_b200_matmul_q8_silu_workspace(m, inter, n)
+    ws = workspace if workspace is not None else _workspace(gate_up.device, need)
+    check(lib.accel_b200_matmul_q8_silu(_p(gate_up), gate_up.stride(0), inter, ctypes.byref(plane), _p(c), c.stride(0),
+                                        m, n, None if epilogue is None else ctypes.byref(epilogue), _p(ws),
+                                        0 if ws is None else ws.numel(), _s()))
+    return c
+
+
 def matmul_f32(a, b, epilogue=None, out=None):
     lib = load()
     m, k = a.shape
@@ -213,6 +230,23 @@ def decode_attention(qkv, row_pos, heads, kv_heads, cos_t, sin_t, k_cache, v_cac
     check(load().accel_b200_decode_attention(_p(qkv), qkv.stride(0), _p(row_seq), _p(row_pos), rows, heads, kv_heads,
                                              64, _p(cos_t), _p(sin_t), ctx, _p(k_cache), _p(v_cache),
                                              kv_heads * ctx * 64, ctx * 64, _p(out), out.stride(0), _p(status), _s()))
+    return out
+
+
+def attention_prefill(q, k_cache, v_cache, first, count, pos0, heads, kv_heads, out=None, max_rows=None):
+    """Tiled causal prefill attention. q [rows, heads * 64] (roped); caches
+    head-major [slots, kv_heads, context, 64]; first/count/pos0 int32 [batch]
+    device tensors."""
+    rows = q.shape[0]
+    ctx = k_cache.shape[2]
+    if out is None:
+        out = torch.zeros(rows, heads * 64, dtype=torch.float32, device=q.device)
+    batch = first.shape[0]
+    if max_rows is None:
+        max_rows = int(count.max().item()) if batch else 0
+    check(load().accel_b200_attention_prefill(_p(q), q.stride(0), _p(k_cache), _p(v_cache), kv_heads * ctx * 64,
+                                              ctx * 64, _p(out), out.stride(0), _p(first), _p(count), _p(pos0), batch,
+                                              max_rows, heads, kv_heads, 64, _s()))
     return out
 
 

@@ -1,7 +1,7 @@
 """Times single kernels of the backend on fixed cases, for profiling.
 
     python -m accelep_b200.profile_cases gemm [--path tc|simt] [--shapes decode|prefill|c5|all]
-    python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280] [--kind fused|split]
+    python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280] [--kind fused|split|prefill]
     python -m accelep_b200.profile_cases list
 
 Each case is launched `reps` times from one captured CUDA graph (no host
@@ -76,6 +76,20 @@ def attention_case(batch, length, reps, kind="fused", context=2048, heads=9, kv_
     kc = [torch.randn(batch, kv_heads, context, head_dim, device="cuda") for _ in range(copies)]
     vc = [torch.randn(batch, kv_heads, context, head_dim, device="cuda") for _ in range(copies)]
     stream = torch.cuda.Stream()
+    if kind == "prefill":
+        # `batch` prompts of `length` rows each, attending causally.
+        rows = batch * length
+        q = torch.randn(rows, heads * head_dim, device="cuda")
+        first = torch.arange(batch, dtype=torch.int32, device="cuda") * length
+        count = torch.full((batch,), length, dtype=torch.int32, device="cuda")
+        pos0 = torch.zeros(batch, dtype=torch.int32, device="cuda")
+        out = torch.zeros(rows, heads * head_dim, device="cuda")
+        with torch.cuda.stream(stream):
+            us = _time_graph(lambda i: K.attention_prefill(q, kc[i % copies], vc[i % copies], first, count, pos0, heads,
+                                                           kv_heads, out=out, max_rows=length), reps, stream)
+        flops = 4.0 * batch * heads * head_dim * length * (length + 1) / 2
+        return {"case": f"attention_prefill_b{batch}_len{length}", "us": round(us, 3),
+                "tflops": round(flops / us / 1e6, 2)}
     if kind == "fused":
         qkv = torch.randn(batch, (heads + 2 * kv_heads) * head_dim, device="cuda")
         pos = torch.full((batch,), length - 1, dtype=torch.int32, device="cuda")
@@ -106,7 +120,7 @@ def main():
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--len", type=int, default=1280)
     ap.add_argument("--reps", type=int, default=50)
-    ap.add_argument("--kind", default="fused", choices=["fused", "split"])
+    ap.add_argument("--kind", default="fused", choices=["fused", "split", "prefill"])
     ap.add_argument("--only", default="", help="run one named gemm case")
     args = ap.parse_args()
     if args.what == "list":

@@ -174,6 +174,20 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
                                         const accel_b200_epilogue* ep, void* workspace, size_t workspace_bytes,
                                         void* stream);
 
+/* c[m, n] = epilogue(SiluMul(gate_up) @ dequant(b)) for fused gate|up rows:
+   row r of the product's A is silu(g) * u with g = gate_up[r * ld + i] and
+   u = gate_up[r * ld + inter + i], i < inter (src/sim_silu.cc:8-13 followed by
+   the down projection, src/llama_model.cc:239-240), so k = inter. The SiluMul
+   value is rounded exactly as accel_b200_silu_mul_rows rounds it; the
+   product and epilogue are those of accel_b200_matmul_q8. `workspace` holds
+   accel_b200_matmul_q8_silu_workspace(m, inter, n) bytes whose first 64 KiB
+   are zero (the same rule as accel_b200_matmul_q8). */
+ACCEL_B200_API size_t accel_b200_matmul_q8_silu_workspace(int64_t m, int64_t inter, int64_t n);
+ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, int64_t inter,
+                                             const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
+                                             int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                                             size_t workspace_bytes, void* stream);
+
 /* fp32 weights with the same fused epilogue and split-K scheme: the fast
    (fused multiply-add, reassociated) product the Llama engine uses. */
 ACCEL_B200_API size_t accel_b200_matmul_f32_workspace(int64_t m, int64_t k, int64_t n);
@@ -211,6 +225,22 @@ ACCEL_B200_API int accel_b200_attention_rows(const float* q, int64_t q_row_strid
                                              float* out, int64_t out_row_stride, const int32_t* row_seq,
                                              const int32_t* row_pos, int64_t rows, int32_t heads, int32_t kv_heads,
                                              int32_t head_dim, void* stream);
+
+/* Causal attention of prefill rows, tiled (src/sim_attend.cc:9-46 over the
+   prompt rows of `batch` sequences, src/llama_model.cc:233). The rows of
+   sequence b are q rows first[b] .. first[b] + count[b] - 1 (device arrays)
+   at positions pos0[b] + i, attending to cache rows [0, pos0[b] + i] of slot
+   b; max_rows >= every count[b]. head_dim 64, at most 4 query heads per kv
+   head; the cache is head-major as in accel_b200_decode_attention (rows of
+   64 floats, element (s, g, t, d) at s * seq_stride + g * head_stride + t * 64
+   + d) and already holds the roped keys of these rows. Agrees with
+   accel_b200_attention_rows within 1e-4. */
+ACCEL_B200_API int accel_b200_attention_prefill(const float* q, int64_t q_stride, const float* k_cache,
+                                                const float* v_cache, int64_t seq_stride, int64_t head_stride,
+                                                float* out, int64_t out_stride, const int32_t* first,
+                                                const int32_t* count, const int32_t* pos0, int32_t batch,
+                                                int32_t max_rows, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                                void* stream);
 
 /* Split-KV decode attention, head_dim 64: one query row per sequence b over
    cache rows [0, lens[b]) of slot b (1 <= lens[b] <= max_len; cache strides

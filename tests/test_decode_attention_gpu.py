@@ -113,3 +113,33 @@ def test_decode_attention_rejects(lib, cuda):
         K.decode_attention(q, pos, 9, 4, cs, cs, kc, kc)  # 9 heads over 4 kv heads
     with pytest.raises(B200Error):
         K.decode_attention(torch.zeros(2, 100, device="cuda"), pos, 9, 3, cs, cs, kc, kc)  # row stride too small
+
+
+@pytest.mark.parametrize("heads,kvh,counts,pos0", [
+    (9, 3, [512, 37, 1, 64, 130], [0, 0, 0, 5, 200]),
+    (4, 2, [96, 33], [0, 1000]),
+    (4, 4, [65], [3]),
+    (8, 2, [40, 7], [0, 60]),
+])
+def test_prefill_attention_matches(lib, cuda, orc, heads, kvh, counts, pos0):
+    """Tiled prefill attention (accel_b200_attention_prefill) against the
+    checker's Attention per sequence: ragged prompts, query tiles that end
+    mid-tile, continuation at a position offset (ForwardIds after earlier
+    rows), and every supported group size."""
+    hd = 64
+    rng = np.random.default_rng(sum(counts) + heads)
+    ctx = max(p + c for p, c in zip(pos0, counts)) + 7
+    batch = len(counts)
+    first = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int32)
+    rows = int(sum(counts))
+    q = rng.standard_normal((rows, heads * hd), dtype=np.float32)
+    kc = rng.standard_normal((batch, kvh, ctx, hd), dtype=np.float32)
+    vc = rng.standard_normal((batch, kvh, ctx, hd), dtype=np.float32)
+    got = H(K.attention_prefill(T(q), T(kc), T(vc), T(first), T(np.array(counts, np.int32)),
+                                T(np.array(pos0, np.int32)), heads, kvh))
+    for b in range(batch):
+        n, p = counts[b], pos0[b]
+        k_ref = np.ascontiguousarray(kc[b, :, :p + n].transpose(1, 0, 2))
+        v_ref = np.ascontiguousarray(vc[b, :, :p + n].transpose(1, 0, 2))
+        want = orc.attend(q[first[b]:first[b] + n].reshape(n, heads, hd), k_ref, v_ref, n, p, heads, kvh, hd)
+        close(got[first[b]:first[b] + n], want.reshape(n, -1))

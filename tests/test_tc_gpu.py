@@ -77,3 +77,35 @@ def test_tc_scalar_scale_and_repeat(lib, cuda, orc):
     mag = np.abs(x).astype(np.float64) @ np.abs(w.astype(np.float64)) * 0.004
     check_close(first, want, 1536, mag)
     assert not H(ws[:256]).any()
+
+
+@pytest.mark.parametrize("m,inter,n", [(1, 1536, 576), (32, 1536, 576), (40, 256, 384), (100, 320, 128),
+                                       (7, 100, 336)])
+def test_silu_product_matches_checker(lib, cuda, orc, m, inter, n):
+    """SiluMul rows feeding the product (accel_b200_matmul_q8_silu): the
+    in-kernel SiluMul of the fp32-tile path (m <= 64), the split pass of the
+    planes path (m > 64), and the CUDA-core path (inter not a multiple of 4
+    or 8 goes there too), each against SiluMul + MatMul of the checker."""
+    rng = np.random.default_rng(m * inter + n)
+    gu = rng.standard_normal((m, 2 * inter), dtype=np.float32) * 2
+    _, w, s = syn.int8_gemm(1, inter, n, m + n)
+    res = rng.standard_normal((m, n), dtype=np.float32)
+    act = orc.silu_mul(np.ascontiguousarray(gu[:, :inter]), np.ascontiguousarray(gu[:, inter:]))
+    want = orc.execute_matmul_q(act, w, s, residual=res)
+    mag = np.abs(act).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
+    for path in (0, 1):
+        K.set_q8_path(path)
+        ep = K.make_epilogue(residual=T(res))
+        got = H(K.matmul_q8_silu(T(gu), T(w), T(s), epilogue=ep))
+        check_close(got, want, inter, mag)
+
+
+def test_fp32_tile_product_every_row_count(lib, cuda, orc):
+    """m = 1 .. 64 on the fp32-tile path (R = 32 and 64, ragged row tiles)."""
+    x, w, s = syn.int8_gemm(64, 576, 256, 11)
+    xt, wt, st = T(x), T(w), T(s)
+    want = orc.execute_matmul_q(x, w, s)
+    mag = np.abs(x).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
+    for m in (1, 2, 31, 32, 33, 63, 64):
+        got = H(K.matmul_q8(xt[:m].contiguous(), wt, st))
+        check_close(got, want[:m], 576, mag[:m])
