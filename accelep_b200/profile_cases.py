@@ -2,6 +2,7 @@
 
     python -m accelep_b200.profile_cases gemm [--path tc|simt] [--shapes decode|prefill|c5|all]
     python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280] [--kind fused|split|prefill]
+    python -m accelep_b200.profile_cases step [--reps 3]
     python -m accelep_b200.profile_cases list
 
 Each case is launched `reps` times from one captured CUDA graph (no host
@@ -68,6 +69,65 @@ def gemm_case(name, m, k, n, reps, copies=None):
             "tflops": round(2 * m * k * n / us / 1e6, 2), "weight_copies": copies}
 
 
+def decode_products(batch=32, layers=30, hidden=576, inter=1536, q_out=576, kv_out=192, vocab=49152, seed=5):
+    """The int8 products of one decode step of the C4 model: per layer the
+    fused q|k|v projection, the output projection (+ residual), the fused
+    gate|up projection and the down projection fed by SiluMul rows (+
+    residual), then the LM head; synthetic weights of the same shapes.
+    Returns (launch(i), algorithmic bytes per step, launches per step): the
+    algorithmic bytes of a product are its int8 weights, scales, fp32 A rows
+    read, C rows written and residual rows read."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+
+    def plane(k, n):
+        w = torch.randint(-127, 128, (k, n), dtype=torch.int8, device="cuda", generator=g)
+        s = torch.rand(n, device="cuda", generator=g) * 1e-3 + 1e-4
+        return w, s
+
+    layers_w = [(plane(hidden, q_out + 2 * kv_out), plane(q_out, hidden), plane(hidden, 2 * inter),
+                 plane(inter, hidden)) for _ in range(layers)]
+    head = plane(hidden, vocab)
+    x = torch.randn(batch, hidden, device="cuda")
+    attn = torch.randn(batch, q_out, device="cuda")
+    qkv = torch.empty(batch, q_out + 2 * kv_out, device="cuda")
+    gu = torch.randn(batch, 2 * inter, device="cuda")
+    hid = torch.randn(batch, hidden, device="cuda")
+    logits = torch.empty(batch, vocab, device="cuda")
+    lib = K.load()
+    need = max(lib.accel_b200_matmul_q8_workspace(batch, hidden, vocab),
+               lib.accel_b200_matmul_q8_silu_workspace(batch, inter, hidden))
+    work = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    res = K.make_epilogue(residual=hid)
+    out_h = torch.empty(batch, hidden, device="cuda")
+
+    def launch(_):
+        for (wqkv, wo, wgu, wd) in layers_w:
+            K.matmul_q8(x, wqkv[0], wqkv[1], out=qkv, workspace=work)
+            K.matmul_q8(attn, wo[0], wo[1], epilogue=res, out=out_h, workspace=work)
+            K.matmul_q8(x, wgu[0], wgu[1], out=gu, workspace=work)
+            K.matmul_q8_silu(gu, wd[0], wd[1], epilogue=res, out=out_h, workspace=work)
+        K.matmul_q8(x, head[0], head[1], out=logits, workspace=work)
+
+    def nbytes(m, k, n, residual=False):
+        return k * n + 4 * n + 4 * m * k + 4 * m * n + (4 * m * n if residual else 0)
+
+    down = inter * hidden + 4 * hidden + 4 * batch * 2 * inter + 8 * batch * hidden  # reads gate|up rows
+    per_layer = (nbytes(batch, hidden, q_out + 2 * kv_out) + nbytes(batch, q_out, hidden, True) +
+                 nbytes(batch, hidden, 2 * inter) + down)
+    total = layers * per_layer + nbytes(batch, hidden, vocab)
+    launch._keep = (layers_w, head, x, attn, qkv, gu, hid, logits, work, res, out_h)
+    return launch, total, 4 * layers + 1
+
+
+def step_case(reps):
+    stream = torch.cuda.Stream()
+    launch, nbytes, count = decode_products()
+    with torch.cuda.stream(stream):
+        us = _time_graph(launch, reps, stream)
+    return {"case": "decode_step_products", "launches": count, "us_per_step": round(us, 2),
+            "us_per_launch": round(us / count, 3), "bytes_per_step": nbytes, "gbs": round(nbytes / us / 1e3, 1)}
+
+
 def attention_case(batch, length, reps, kind="fused", context=2048, heads=9, kv_heads=3, head_dim=64):
     """Decode attention of `batch` sequences at context length `length` over
     head-major caches: the fused step (Rope, AppendCache, attention) or the
@@ -114,7 +174,7 @@ def attention_case(batch, length, reps, kind="fused", context=2048, heads=9, kv_
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "list"])
+    ap.add_argument("what", choices=["gemm", "attention", "step", "list"])
     ap.add_argument("--path", default="tc", choices=["tc", "simt"])
     ap.add_argument("--shapes", default="decode", choices=["decode", "prefill", "c5", "all"])
     ap.add_argument("--batch", type=int, default=32)
@@ -137,6 +197,8 @@ def main():
                 reps = args.reps if m * k * n < 1e10 else max(3, args.reps // 10)
                 print(json.dumps(dict(gemm_case(name, m, k, n, reps), path=args.path)), flush=True)
         K.set_q8_path(0)
+    elif args.what == "step":
+        print(json.dumps(step_case(args.reps)), flush=True)
     else:
         print(json.dumps(attention_case(args.batch, args.len, args.reps, args.kind)), flush=True)
 

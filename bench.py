@@ -43,6 +43,11 @@ WEIGHT_SEED = 4
 PROMPT_SEED = 41
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
+# DRAM bytes (read + write) per launch from ncu captures of the same launches
+# (profiles/q8_product_decode_step.md, profiles/decode_attention_b32_len1280.md);
+# None until captured.
+PRODUCT_TRAFFIC = None
+ATTENTION_TRAFFIC = 63_521_280
 
 
 def config(n):
@@ -206,18 +211,55 @@ def attention_roofline(torch, stream, batch=SEQS, length=1280, reps=50):
 
         for i in range(3):
             launch(i)
+        torch.cuda.synchronize()
+        # `reps` launches in one CUDA graph (as the engine replays them), so
+        # host launch overhead stays out of the per-launch time.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(reps):
+                launch(i)
+        graph.replay()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         start.record(stream)
-        for i in range(reps):
-            launch(i)
+        graph.replay()
         end.record(stream)
         end.synchronize()
+        del graph
     sec = start.elapsed_time(end) / 1000.0 / reps
     nbytes = batch * (length - 1) * 2 * kvd * 4 + batch * 2 * kvd * 4 + batch * (heads + 2 * kvh) * hd * 4 + \
         batch * heads * hd * 4
     del kc, vc
     return nbytes / sec / 1e9, sec, nbytes
+
+
+def products_roofline(torch, stream, reps=3):
+    """Times the decode step's 121 int8 products (C4 shapes, synthetic weights)
+    replayed from one CUDA graph, with CUDA events on the launching stream;
+    returns (algorithmic GB/s, seconds per launch, bytes per launch) averaged
+    over the step's launches."""
+    from accelep_b200 import profile_cases as PC
+
+    with torch.cuda.stream(stream):
+        launch, nbytes, count = PC.decode_products()
+        for i in range(2):
+            launch(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch(0)
+        graph.replay()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        del graph, launch
+    sec = start.elapsed_time(end) / 1000.0 / reps / count
+    per_launch = nbytes / count
+    return per_launch / sec / 1e9, sec, per_launch
 
 
 def run_b200(args):
@@ -284,6 +326,7 @@ def run_b200(args):
     if rank == 0:
         peak, peak_kind = hbm_peak()
         achieved, sec, nbytes = attention_roofline(torch, stream)
+        p_achieved, p_sec, p_bytes = products_roofline(torch, stream)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cores = 1
@@ -301,11 +344,16 @@ def run_b200(args):
                 "e2e": {"value": tokens / wall, "unit": UNIT, "h2d_bytes_per_step": SEQS * prompt_len * 4,
                         "d2h_bytes_per_step": SEQS * new * 4},
                 "gpu_launches": int(launches),
-                "roofline": {"kernel": "decode_attention (fused Rope+AppendCache+attention, B=32, 1280 context rows)",
-                             "bound": "hbm",
-                             "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                             "frac": achieved / peak, "traffic": None,
-                             "bytes_per_launch": nbytes, "us_per_launch": sec * 1e6},
+                "roofline": {"kernel": "Q8GemmTcKernel: the decode step's 121 int8 products (largest share of the "
+                                       "step), graph-replayed, per-launch average", "bound": "hbm",
+                             "achieved": p_achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                             "frac": p_achieved / peak, "traffic": PRODUCT_TRAFFIC,
+                             "bytes_per_launch": p_bytes, "us_per_launch": p_sec * 1e6},
+                "roofline_attention": {"kernel": "decode_attention (fused Rope+AppendCache+attention, B=32, 1280 "
+                                                 "context rows)", "bound": "hbm",
+                                       "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                                       "frac": achieved / peak, "traffic": ATTENTION_TRAFFIC,
+                                       "bytes_per_launch": nbytes, "us_per_launch": sec * 1e6},
                 "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line), flush=True)
     model.close()
