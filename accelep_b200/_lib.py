@@ -64,6 +64,9 @@ SIGNATURES = {
     "accel_b200_matmul_q8_silu_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_q8_silu": (c_int, [c_vp, c_i64, c_i64, P_plane, c_vp, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz,
                                           c_vp]),
+    "accel_b200_matmul_q8_rmsnorm_workspace": (c_sz, [c_i64, c_i64, c_i64]),
+    "accel_b200_matmul_q8_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_f32, P_plane, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                             P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_matmul_f32_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_f32": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_rope_append": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,

@@ -341,9 +341,11 @@ int EmptySum(float* c, int64_t ldc, int64_t m, int64_t n, const Epilogue& ep, cu
 bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
                 int64_t n);
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n);
-int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale,
-          float* c, int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace,
-          size_t workspace_bytes, int32_t* status, cudaStream_t stream);
+int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
+          const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
+          const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream);
+int LaunchRmsNormRows(const float* x, int64_t ldx, const float* w, float* y, int64_t ldy, int64_t rows, int64_t dim,
+                      float eps, int64_t row_offset, cudaStream_t stream);
 int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
                       cudaStream_t stream);
 
@@ -406,8 +408,8 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
   }
   const int8_t* w = b->q + b->offset;
   if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
-    return RunTc(a, nullptr, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace, workspace_bytes,
-                 nullptr, AsStream(stream));
+    return RunTc(a, nullptr, lda, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace,
+                 workspace_bytes, nullptr, AsStream(stream));
   }
   g.a = a;
   g.lda = lda;
@@ -452,8 +454,8 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
   const float* up = gate_up + inter;
   if (inter % 4 == 0 && UseTc(gate_up, ld, w, b->axis, b->zero, m, inter, n) &&
       reinterpret_cast<uintptr_t>(up) % 16 == 0) {
-    return RunTc(gate_up, up, ld, w, b->scale, b->axis < 0, c, ldc, m, inter, n, e, workspace, workspace_bytes,
-                 nullptr, AsStream(stream));
+    return RunTc(gate_up, up, ld, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, inter, n, e, workspace,
+                 workspace_bytes, nullptr, AsStream(stream));
   }
   // CUDA cores: SiluMul rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * inter * sizeof(float);
@@ -461,6 +463,46 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
   const int rc = LaunchSiluMulRows(gate_up, ld, act, inter, m, inter, AsStream(stream));
   if (rc != ACCEL_B200_OK) return rc;
   return accel_b200_matmul_q8(act, inter, b, c, ldc, m, inter, n, ep, workspace, base, stream);
+}
+
+ACCEL_B200_API size_t accel_b200_matmul_q8_rmsnorm_workspace(int64_t m, int64_t k, int64_t n) {
+  // The product's workspace, then room for the normalized rows when the
+  // product runs on the CUDA cores.
+  const size_t base = (accel_b200_matmul_q8_workspace(m, k, n) + 255) / 256 * 256;
+  return base + static_cast<size_t>(m > 0 ? m : 0) * static_cast<size_t>(k > 0 ? k : 0) * sizeof(float);
+}
+
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, const float* gamma, float eps,
+                                                const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
+                                                int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+  if (m < 0 || k < 0 || n < 0 || b == nullptr || ldx < k) {
+    return SetError(ACCEL_B200_EINVAL, "quantized MatMul (RmsNorm rows) is out of range");
+  }
+  if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
+  Epilogue e{};
+  if (!ToEpilogue(ep, &e)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
+  if (m == 0 || n == 0) return ClearError();
+  if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
+  if (k == 0) return EmptySum(c, ldc, m, n, e, AsStream(stream));
+  if (x == nullptr || gamma == nullptr || b->q == nullptr || b->scale == nullptr) {
+    return SetError(ACCEL_B200_EINVAL, "quantized MatMul is missing an operand");
+  }
+  const size_t need = accel_b200_matmul_q8_rmsnorm_workspace(m, k, n);
+  if (workspace == nullptr || workspace_bytes < need) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_rmsnorm: workspace too small");
+  }
+  const int8_t* w = b->q + b->offset;
+  if (UseTc(x, ldx, w, b->axis, b->zero, m, k, n) && reinterpret_cast<uintptr_t>(gamma) % 16 == 0) {
+    return RunTc(x, nullptr, ldx, gamma, eps, w, b->scale, b->axis < 0, c, ldc, m, k, n, e, workspace,
+                 workspace_bytes, nullptr, AsStream(stream));
+  }
+  // CUDA cores: RmsNorm rows into the workspace's tail, then the product.
+  const size_t base = need - static_cast<size_t>(m) * k * sizeof(float);
+  float* act = reinterpret_cast<float*>(static_cast<char*>(workspace) + base);
+  const int rc = LaunchRmsNormRows(x, ldx, gamma, act, k, m, k, eps, 0, AsStream(stream));
+  if (rc != ACCEL_B200_OK) return rc;
+  return accel_b200_matmul_q8(act, k, b, c, ldc, m, k, n, ep, workspace, base, stream);
 }
 
 ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const float* b, float* c, int64_t ldc, int64_t m,

@@ -73,7 +73,7 @@ constexpr int kConvWarps = 4;
 constexpr int kThreads = (2 + kConvWarps) * 32;
 constexpr int kMaxStages = 4;
 
-enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2 };
+enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2, kANorm = 3 };
 
 template <int R, int S, int M>
 struct Tc {
@@ -91,6 +91,10 @@ struct Tc {
 };
 
 struct TcArgs {
+  const float* a;      // fp32 A rows (norm mode: the whole rows are read for their RMS)
+  int64_t lda;
+  const float* gamma;  // norm mode: RmsNorm weights [k]
+  float eps;
   int64_t m, k, n;
   int32_t kb_total;
   int32_t kb_per_split;
@@ -181,9 +185,13 @@ __device__ __forceinline__ float SiluMul(float g, float u) {
 // planes in the K-major 128-byte-swizzled layout the planes TMA would write:
 // plane p, row r at p * R * 128 + r * 128, 16-byte chunk j stored at
 // j ^ (r % 8). Each thread takes four consecutive k of one row per pass.
-// Rows at or past `valid` are skipped: their planes stay zero.
+// Rows at or past `valid` are skipped: their planes stay zero. Norm mode: the
+// element is RmsNorm'd first, float(double(x) * inv[row]) * gamma[k], as
+// RmsNormKernel rounds it (gamma points at this block's first k; `kvalid` k
+// of the block lie inside the matrix).
 template <int R, int M>
-__device__ __forceinline__ void SplitTile(const uint8_t* raw, uint8_t* planes, int ct, int valid) {
+__device__ __forceinline__ void SplitTile(const uint8_t* raw, uint8_t* planes, int ct, int valid,
+                                          const float* gamma, int kvalid, const double* inv) {
 #pragma unroll
   for (int pass = 0; pass < R * 16 / (kConvWarps * 32); ++pass) {
     const int idx = pass * (kConvWarps * 32) + ct;
@@ -198,6 +206,14 @@ __device__ __forceinline__ void SplitTile(const uint8_t* raw, uint8_t* planes, i
       x[1] = SiluMul(v.y, u.y);
       x[2] = SiluMul(v.z, u.z);
       x[3] = SiluMul(v.w, u.w);
+    } else if constexpr (M == kANorm) {
+      const float4 w = k4 * 4 < kvalid ? __ldg(reinterpret_cast<const float4*>(gamma + k4 * 4))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      const double iv = inv[row];
+      x[0] = __fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), w.x);
+      x[1] = __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), w.y);
+      x[2] = __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), w.z);
+      x[3] = __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), w.w);
     } else {
       x[0] = v.x;
       x[1] = v.y;
@@ -211,6 +227,59 @@ __device__ __forceinline__ void SplitTile(const uint8_t* raw, uint8_t* planes, i
     *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(h[0], h[1]), PackBf16(h[2], h[3]));
     *reinterpret_cast<uint2*>(planes + R * 128 + off) = make_uint2(PackBf16(md[0], md[1]), PackBf16(md[2], md[3]));
     *reinterpret_cast<uint2*>(planes + 2 * R * 128 + off) = make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+  }
+}
+
+// 1 / sqrt(mean(x^2) + eps) of a row in double, summed exactly as
+// RmsNormKernel sums it (lane-strided partial sums, then a butterfly), so the
+// normalized values are bit-identical to that kernel's.
+__device__ __forceinline__ double RowInverseRms(const float* in, int64_t dim, float eps, int lane) {
+  double sq = 0.0;
+#pragma unroll 6
+  for (int64_t i = lane; i < dim; i += 32) {
+    const double v = static_cast<double>(in[i]);
+    sq += v * v;
+  }
+  sq = WarpSum(sq);
+  return 1.0 / sqrt(sq / static_cast<double>(dim) + static_cast<double>(eps));
+}
+
+// The same inverse RMS for rows [0, valid) of a tile, all rows at once: four
+// converter threads per row (ct = 4 * row + q) and the same arithmetic order.
+// RmsNormKernel's lane l sums x[l + 32 i] over i ascending and the 32 partial
+// sums combine in a butterfly (xor 16, 8, 4, 2, 1; each level a + b in either
+// order, which is exact-commutative). Here thread q holds the partials of
+// lanes 8q .. 8q + 7, so levels 16 and 8 are shuffles with threads q ^ 2 and
+// q ^ 1 and levels 4, 2, 1 stay inside the thread. dim % 8 == 0.
+template <int R>
+__device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int64_t row0, int valid, int64_t dim,
+                                               float eps, int ct, double* inv) {
+  for (int base = 0; base < R; base += kConvWarps * 8) {
+    const int r = base + (ct >> 2), q = ct & 3;
+    double s[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] = 0.0;
+    if (r < valid) {
+      const float* in = a + (row0 + r) * lda + 8 * q;
+#pragma unroll 6
+      for (int64_t i0 = 0; i0 + 8 * q < dim; i0 += 32) {
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(in + i0));
+        const float4 x1 = __ldg(reinterpret_cast<const float4*>(in + i0 + 4));
+        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const double v = static_cast<double>(xs[j]);
+          s[j] += v * v;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] += __shfl_xor_sync(kFull, s[j], 2);  // lane l ^ 16
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j] += __shfl_xor_sync(kFull, s[j], 1);  // lane l ^ 8
+    const double u0 = s[0] + s[4], u1 = s[1] + s[5], u2 = s[2] + s[6], u3 = s[3] + s[7];  // l ^ 4
+    const double sum = (u0 + u2) + (u1 + u3);                                             // l ^ 2, l ^ 1
+    if (r < valid && q == 0) inv[r] = 1.0 / sqrt(sum / static_cast<double>(dim) + static_cast<double>(eps));
   }
 }
 
@@ -231,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       cempty[kConvBufs], accf;
   __shared__ uint32_t tmem_s;
   __shared__ int32_t ok_s;
+  __shared__ double inv_s[M == kANorm ? R : 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t raw_addr = SmemAddr(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
@@ -338,6 +408,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if constexpr (M == kANorm) {
+      // Row RMS of the valid rows (whole rows of A).
+      PdlWait();
+      TileInverseRms<R>(g.a, g.lda, row0, valid, g.k, g.eps, ct, inv_s);
+      asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
+    }
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S, c = i % kConvBufs;
       uint8_t* stage = smem + s * L::kStage;
@@ -346,7 +422,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ConvertWeightBlock(stage + L::kXBytes, conv_base + c * kWConv, ct);
       if constexpr (M != kAPlanes) {
         ok &= MbarWait(&full_x[s], (i / S) & 1);
-        SplitTile<R, M>(stage + L::kXBytes + kWRaw, stage, ct, valid);
+        const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBk;
+        SplitTile<R, M>(stage + L::kXBytes + kWRaw, stage, ct, valid, M == kANorm ? g.gamma + k0 : nullptr,
+                        static_cast<int>(Min64(kBk, g.k - k0)), inv_s);
       }
       FenceProxyAsyncSmem();
       __syncwarp();
@@ -491,6 +569,38 @@ __global__ void SplitPlanesKernel(const float* __restrict__ a, const float* __re
   }
 }
 
+// RmsNorm rows then split: one warp per row computes the row's inverse RMS as
+// RmsNormKernel does and writes the three planes of float(double(x) * inv) * w.
+__global__ void SplitPlanesNormKernel(const float* __restrict__ a, int64_t lda, const float* __restrict__ gamma,
+                                      float eps, int64_t m, int64_t k, __nv_bfloat16* __restrict__ planes) {
+  PdlTrigger();
+  PdlWait();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t plane = m * k;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+    const float* in = a + r * lda;
+    const double iv = RowInverseRms(in, k, eps, lane);
+    for (int64_t q = lane; q < k / 4; q += 32) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(in + q * 4));
+      const float4 w = __ldg(reinterpret_cast<const float4*>(gamma + q * 4));
+      const float x[4] = {__fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), w.x),
+                          __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), w.y),
+                          __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), w.z),
+                          __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), w.w)};
+      float hi[4], mid[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Split3(x[i], &hi[i], &mid[i], &lo[i]);
+      const int64_t off = r * k + q * 4;
+      *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(hi[0], hi[1]), PackBf16(hi[2], hi[3]));
+      *reinterpret_cast<uint2*>(planes + plane + off) =
+          make_uint2(PackBf16(mid[0], mid[1]), PackBf16(mid[2], mid[3]));
+      *reinterpret_cast<uint2*>(planes + 2 * plane + off) =
+          make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+    }
+  }
+}
+
 struct TcPlan {
   int r;
   int mode;  // AMode
@@ -507,7 +617,7 @@ constexpr int MaxStages() {
   return stage * 4 + kConvBufs * kWConv + 1024 <= 227 * 1024 ? 4 : 3;
 }
 
-TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu) {
+TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   TcPlan p{};
   p.r = m <= 32 ? 32 : (m <= 64 ? 64 : 128);
   p.feature_tiles = CeilDiv(n, kBn);
@@ -528,7 +638,7 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu) {
   // Splitting fp32 tiles in the kernel saves the planes pass (one launch) but
   // adds converter work to every k block: worth it for CTAs that walk few
   // blocks (latency-bound decode products), not for long weight streams.
-  p.mode = p.r == 128 || p.kb_per_split > 4 ? kAPlanes : (silu ? kASilu : kAF32);
+  p.mode = p.r == 128 || p.kb_per_split > 4 ? kAPlanes : (silu ? kASilu : (norm ? kANorm : kAF32));
   p.planes_bytes = p.mode == kAPlanes ? (static_cast<size_t>(3) * m * k * 2 + 1023) / 1024 * 1024 : 0;
   return p;
 }
@@ -596,16 +706,18 @@ bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, cons
 }
 
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
-  const TcPlan p = MakeTcPlan(m, k, n, false);
+  const TcPlan p = MakeTcPlan(m, k, n, false, false);
   return kCounterRegion + p.planes_bytes;
 }
 
 // a: fp32 rows (lda); with `up` set, the product's A is SiluMul(a, up) (same
-// row stride). The caller checked TcEligible for a (and up).
-int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale,
-          float* c, int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, void* workspace,
-          size_t workspace_bytes, int32_t* status, cudaStream_t stream) {
-  const TcPlan p = MakeTcPlan(m, k, n, up != nullptr);
+// row stride); with `gamma` set, A is RmsNorm(a) with weights gamma [k] and
+// eps (a's rows are whole rows of length k). The caller checked TcEligible
+// for a (and up).
+int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
+          const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
+          const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream) {
+  const TcPlan p = MakeTcPlan(m, k, n, up != nullptr, gamma != nullptr);
   if (p.planes_bytes > 0 && (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes)) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
   }
@@ -618,9 +730,14 @@ int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const f
     const int64_t total = m * (k / 4);
     const int64_t blocks = CeilDiv(total, 256);
     const int grid = static_cast<int>(blocks < kSms * 16 ? blocks : kSms * 16);
-    const int rc = CheckLaunchEx(LaunchK(SplitPlanesKernel, dim3(grid), dim3(256), 0, stream, 1u, 1u, a, up, lda, m,
-                                         k, planes),
-                                 "matmul_q8_split");
+    const int rc =
+        gamma != nullptr
+            ? CheckLaunchEx(LaunchK(SplitPlanesNormKernel, dim3(static_cast<unsigned>(Min64(CeilDiv(m, 8), kSms * 16))),
+                                    dim3(256), 0, stream, 1u, 1u, a, lda, gamma, eps, m, k, planes),
+                            "matmul_q8_split_norm")
+            : CheckLaunchEx(LaunchK(SplitPlanesKernel, dim3(grid), dim3(256), 0, stream, 1u, 1u, a, up, lda, m, k,
+                                    planes),
+                            "matmul_q8_split");
     if (rc != ACCEL_B200_OK) return rc;
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m), 3};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) * 2, static_cast<cuuint64_t>(m) * k * 2};
@@ -642,6 +759,10 @@ int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const f
     if (up == nullptr) tu = tx;
   }
   TcArgs g{};
+  g.a = a;
+  g.lda = lda;
+  g.gamma = gamma;
+  g.eps = eps;
   g.m = m;
   g.k = k;
   g.n = n;
@@ -663,6 +784,10 @@ int RunTc(const float* a, const float* up, int64_t lda, const int8_t* w, const f
   if (p.mode == kASilu) {
     return p.r == 32 ? LaunchTcStages<32, kASilu>(tw, tx, tu, g, p, stream)
                      : LaunchTcStages<64, kASilu>(tw, tx, tu, g, p, stream);
+  }
+  if (p.mode == kANorm) {
+    return p.r == 32 ? LaunchTcStages<32, kANorm>(tw, tx, tu, g, p, stream)
+                     : LaunchTcStages<64, kANorm>(tw, tx, tu, g, p, stream);
   }
   return p.r == 32 ? LaunchTcStages<32, kAF32>(tw, tx, tu, g, p, stream)
                    : LaunchTcStages<64, kAF32>(tw, tx, tu, g, p, stream);

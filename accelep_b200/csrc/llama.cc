@@ -587,8 +587,14 @@ class Engine {
       for (const Layer& l : layers) {
         for (const Group* g : {&l.qkv, &l.o, &l.gu, &l.down}) ws = std::max(ws, GemmWorkspace(*g, m));
         if (l.down.kind == WKind::Q8) ws = std::max(ws, accel_b200_matmul_q8_silu_workspace(m, l.down.k, l.down.n));
+        for (const Group* g : {&l.qkv, &l.gu}) {
+          if (g->kind == WKind::Q8) ws = std::max(ws, accel_b200_matmul_q8_rmsnorm_workspace(m, g->k, g->n));
+        }
       }
       ws = std::max(ws, GemmWorkspace(lm_head, std::min<int64_t>(m, seqs)));
+      if (lm_head.kind == WKind::Q8) {
+        ws = std::max(ws, accel_b200_matmul_q8_rmsnorm_workspace(std::min<int64_t>(m, seqs), lm_head.k, lm_head.n));
+      }
     }
     moved |= gemm_ws.Ensure(ws);
     moved |= status.Ensure(16);
@@ -618,6 +624,21 @@ class Engine {
     }
   }
 
+  // RmsNorm(x) then the product (src/llama_model.cc:228-229, :237-238, :245-246):
+  // one kernel for int8 weights; through `normed` for fp32 weights.
+  void NormGemm(const float* x, const DevBuf& gamma, const Group& g, int64_t m, float* c, int64_t ldc,
+                const accel_b200_epilogue* ep, DevBuf& normed_buf) {
+    const int64_t H = cfg.hidden;
+    if (g.kind == WKind::Q8) {
+      accel_b200_q8_plane plane{g.w.as<int8_t>(), g.scale.as<float>(), nullptr, 0, 1};
+      Abi(accel_b200_matmul_q8_rmsnorm(x, H, gamma.as<float>(), cfg.eps, &plane, c, ldc, m, g.k, g.n, ep, gemm_ws.p,
+                                       gemm_ws.bytes, stream));
+    } else {
+      Abi(accel_b200_rmsnorm(x, gamma.as<float>(), normed_buf.as<float>(), m, H, cfg.eps, 0, stream));
+      Gemm(normed_buf.as<float>(), H, g, m, c, ldc, ep);
+    }
+  }
+
   // src/llama_model.cc:209-247 over `rows` rows of `seqs` sequences. The
   // last row of each sequence gives its logit row. decode: rows == seqs,
   // row b is sequence b's new token at dec_pos[b].
@@ -642,8 +663,7 @@ class Engine {
       Layer& l = layers[static_cast<size_t>(li)];
       float* kc = k_cache[static_cast<size_t>(li)].as<float>();
       float* vc = v_cache[static_cast<size_t>(li)].as<float>();
-      Abi(accel_b200_rmsnorm(hid, l.attn_norm.as<float>(), normed.as<float>(), rows, H, cfg.eps, 0, stream));
-      Gemm(normed.as<float>(), H, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr);
+      NormGemm(hid, l.attn_norm, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr, normed);
       if (decode && head_dim == 64) {
         // Rope, AppendCache and attention of the new rows in one kernel.
         Abi(accel_b200_decode_attention(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
@@ -665,8 +685,7 @@ class Engine {
         }
       }
       Gemm(mixed.as<float>(), q_out, l.o, rows, hid, H, &residual);
-      Abi(accel_b200_rmsnorm(hid, l.post_norm.as<float>(), normed.as<float>(), rows, H, cfg.eps, 0, stream));
-      Gemm(normed.as<float>(), H, l.gu, rows, gu.as<float>(), 2 * I, nullptr);
+      NormGemm(hid, l.post_norm, l.gu, rows, gu.as<float>(), 2 * I, nullptr, normed);
       if (l.down.kind == WKind::Q8) {
         // SiluMul feeds the down projection's operand directly.
         accel_b200_q8_plane plane{l.down.w.as<int8_t>(), l.down.scale.as<float>(), nullptr, 0, 1};
@@ -682,8 +701,7 @@ class Engine {
       Abi(accel_b200_gather_rows(hid, H, last_rows.as<int32_t>(), seqs, H, gathered.as<float>(), H, stream));
       last = gathered.as<float>();
     }
-    Abi(accel_b200_rmsnorm(last, final_norm.as<float>(), normed_last.as<float>(), seqs, H, cfg.eps, 0, stream));
-    Gemm(normed_last.as<float>(), H, lm_head, seqs, logits.as<float>(), cfg.vocab, nullptr);
+    NormGemm(last, final_norm, lm_head, seqs, logits.as<float>(), cfg.vocab, nullptr, normed_last);
     // A captured decode forward is counted once per replay instead.
     if (!decode) NoteKernelMatmuls(static_cast<int64_t>(7) * cfg.layers + 1);
   }

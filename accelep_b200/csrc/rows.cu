@@ -45,14 +45,14 @@ __global__ void EmbedKernel(const int32_t* __restrict__ ids, int64_t id_offset, 
 // One warp per row. Sum of squares in double (src/sim_rmsnorm.cc:11-14), one
 // double reciprocal square root, float(x * inv) * w.
 __global__ void RmsNormKernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ y,
-                              int64_t rows, int64_t dim, float eps, int64_t row_offset) {
+                              int64_t rows, int64_t dim, float eps, int64_t row_offset, int64_t ldx, int64_t ldy) {
   PdlTrigger();
   PdlWait();
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const float* in = x + (row_offset + r) * dim;
-    float* out = y + r * dim;
+    const float* in = x + (row_offset + r) * ldx;
+    float* out = y + r * ldy;
     double sq = 0.0;
     for (int64_t i = lane; i < dim; i += 32) {
       const double v = static_cast<double>(in[i]);
@@ -177,6 +177,15 @@ bool BiasStrides(const int64_t* shape, int rank, int64_t m, int64_t n, int64_t* 
   return false;
 }
 
+// RmsNorm of `rows` rows of length dim: x rows at x + (row_offset + r) * ldx,
+// output rows at y + r * ldy.
+int LaunchRmsNormRows(const float* x, int64_t ldx, const float* w, float* y, int64_t ldy, int64_t rows, int64_t dim,
+                      float eps, int64_t row_offset, cudaStream_t stream) {
+  return CheckLaunchEx(LaunchK(RmsNormKernel, dim3(GridFor(rows, 8, 16)), dim3(256), 0, stream, 1u, 1u, x, w, y, rows,
+                               dim, eps, row_offset, ldx, ldy),
+                       "rmsnorm");
+}
+
 }  // namespace accel_b200
 
 using namespace accel_b200;
@@ -198,9 +207,7 @@ ACCEL_B200_API int accel_b200_rmsnorm(const float* x, const float* weight, float
   if (BadDims(rows, dim, row_offset)) return SetError(ACCEL_B200_EINVAL, "rmsnorm: negative size");
   if (rows == 0 || dim == 0) return ClearError();
   if (x == nullptr || weight == nullptr || y == nullptr) return SetError(ACCEL_B200_EINVAL, "rmsnorm: null pointer");
-  return CheckLaunchEx(LaunchK(RmsNormKernel, dim3(GridFor(rows, 8, 16)), dim3(256), 0, AsStream(stream), 1u, 1u, x,
-                               weight, y, rows, dim, eps, row_offset),
-                       "rmsnorm");
+  return LaunchRmsNormRows(x, dim, weight, y, dim, rows, dim, eps, row_offset, AsStream(stream));
 }
 
 ACCEL_B200_API int accel_b200_rope(float* states, const float* cos_table, const float* sin_table, int64_t seq,

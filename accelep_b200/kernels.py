@@ -179,6 +179,22 @@ def matmul_q8_silu(gate_up, q, scale, axis=1, epilogue=None, out=None, workspace
     return c
 
 
+def matmul_q8_rmsnorm(x, gamma, eps, q, scale, axis=1, epilogue=None, out=None, workspace=None):
+    """RmsNorm(x[:, :k]) @ dequant(q); q holds a [k, n] plane (x's row stride
+    may be wider than k)."""
+    lib = load()
+    m = x.shape[0]
+    k, n = q.shape
+    c = out if out is not None else torch.zeros(m, n, dtype=torch.float32, device=x.device)
+    plane = Q8Plane(q.data_ptr(), scale.data_ptr(), 0, 0, axis)
+    need = lib.accel_b200_matmul_q8_rmsnorm_workspace(m, k, n)
+    ws = workspace if workspace is not None else _workspace(x.device, need)
+    check(lib.accel_b200_matmul_q8_rmsnorm(_p(x), x.stride(0), _p(gamma), eps, ctypes.byref(plane), _p(c), c.stride(0),
+                                           m, k, n, None if epilogue is None else ctypes.byref(epilogue), _p(ws),
+                                           0 if ws is None else ws.numel(), _s()))
+    return c
+
+
 def matmul_f32(a, b, epilogue=None, out=None):
     lib = load()
     m, k = a.shape

@@ -70,10 +70,11 @@ def gemm_case(name, m, k, n, reps, copies=None):
 
 
 def decode_products(batch=32, layers=30, hidden=576, inter=1536, q_out=576, kv_out=192, vocab=49152, seed=5):
-    """The int8 products of one decode step of the C4 model: per layer the
-    fused q|k|v projection, the output projection (+ residual), the fused
-    gate|up projection and the down projection fed by SiluMul rows (+
-    residual), then the LM head; synthetic weights of the same shapes.
+    """The int8 products of one decode step of the C4 model, issued as the
+    engine issues them: per layer the fused q|k|v projection fed by RmsNorm
+    rows, the output projection (+ residual), the fused gate|up projection fed
+    by RmsNorm rows and the down projection fed by SiluMul rows (+ residual),
+    then the LM head fed by RmsNorm rows; synthetic weights of the same shapes.
     Returns (launch(i), algorithmic bytes per step, launches per step): the
     algorithmic bytes of a product are its int8 weights, scales, fp32 A rows
     read, C rows written and residual rows read."""
@@ -94,19 +95,20 @@ def decode_products(batch=32, layers=30, hidden=576, inter=1536, q_out=576, kv_o
     hid = torch.randn(batch, hidden, device="cuda")
     logits = torch.empty(batch, vocab, device="cuda")
     lib = K.load()
-    need = max(lib.accel_b200_matmul_q8_workspace(batch, hidden, vocab),
+    need = max(lib.accel_b200_matmul_q8_rmsnorm_workspace(batch, hidden, vocab),
                lib.accel_b200_matmul_q8_silu_workspace(batch, inter, hidden))
+    gamma = torch.rand(hidden, device="cuda", generator=g) + 0.5
     work = torch.zeros(need, dtype=torch.uint8, device="cuda")
     res = K.make_epilogue(residual=hid)
     out_h = torch.empty(batch, hidden, device="cuda")
 
     def launch(_):
         for (wqkv, wo, wgu, wd) in layers_w:
-            K.matmul_q8(x, wqkv[0], wqkv[1], out=qkv, workspace=work)
+            K.matmul_q8_rmsnorm(x, gamma, 1e-5, wqkv[0], wqkv[1], out=qkv, workspace=work)
             K.matmul_q8(attn, wo[0], wo[1], epilogue=res, out=out_h, workspace=work)
-            K.matmul_q8(x, wgu[0], wgu[1], out=gu, workspace=work)
+            K.matmul_q8_rmsnorm(x, gamma, 1e-5, wgu[0], wgu[1], out=gu, workspace=work)
             K.matmul_q8_silu(gu, wd[0], wd[1], epilogue=res, out=out_h, workspace=work)
-        K.matmul_q8(x, head[0], head[1], out=logits, workspace=work)
+        K.matmul_q8_rmsnorm(x, gamma, 1e-5, head[0], head[1], out=logits, workspace=work)
 
     def nbytes(m, k, n, residual=False):
         return k * n + 4 * n + 4 * m * k + 4 * m * n + (4 * m * n if residual else 0)
@@ -115,7 +117,7 @@ def decode_products(batch=32, layers=30, hidden=576, inter=1536, q_out=576, kv_o
     per_layer = (nbytes(batch, hidden, q_out + 2 * kv_out) + nbytes(batch, q_out, hidden, True) +
                  nbytes(batch, hidden, 2 * inter) + down)
     total = layers * per_layer + nbytes(batch, hidden, vocab)
-    launch._keep = (layers_w, head, x, attn, qkv, gu, hid, logits, work, res, out_h)
+    launch._keep = (layers_w, head, x, attn, qkv, gu, hid, logits, work, res, out_h, gamma)
     return launch, total, 4 * layers + 1
 
 

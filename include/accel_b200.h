@@ -188,6 +188,20 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
                                              int64_t n, const accel_b200_epilogue* ep, void* workspace,
                                              size_t workspace_bytes, void* stream);
 
+/* c[m, n] = epilogue(RmsNorm(x) @ dequant(b)): row r of the product's A is
+   RmsNorm of x row r (length k, row stride ldx) with weights gamma [k] and
+   eps (src/sim_rmsnorm.cc:7-20 followed by the projection, as
+   src/llama_model.cc:228-229 and :237-238 chain them). The normalized values
+   are bit-identical to accel_b200_rmsnorm's; product and epilogue as
+   accel_b200_matmul_q8. `workspace` holds
+   accel_b200_matmul_q8_rmsnorm_workspace(m, k, n) bytes whose first 64 KiB
+   are zero. */
+ACCEL_B200_API size_t accel_b200_matmul_q8_rmsnorm_workspace(int64_t m, int64_t k, int64_t n);
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, const float* gamma, float eps,
+                                                const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
+                                                int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                                                size_t workspace_bytes, void* stream);
+
 /* fp32 weights with the same fused epilogue and split-K scheme: the fast
    (fused multiply-add, reassociated) product the Llama engine uses. */
 ACCEL_B200_API size_t accel_b200_matmul_f32_workspace(int64_t m, int64_t k, int64_t n);

@@ -109,3 +109,28 @@ def test_fp32_tile_product_every_row_count(lib, cuda, orc):
     for m in (1, 2, 31, 32, 33, 63, 64):
         got = H(K.matmul_q8(xt[:m].contiguous(), wt, st))
         check_close(got, want[:m], 576, mag[:m])
+
+
+@pytest.mark.parametrize("m,k,n,ldx", [(32, 576, 960, 576), (33, 576, 576, 600), (32, 576, 49152, 576),
+                                       (100, 576, 384, 576), (1, 1536, 256, 1536), (7, 100, 336, 100)])
+def test_rmsnorm_product(lib, cuda, orc, m, k, n, ldx):
+    """RmsNorm rows feeding the product (accel_b200_matmul_q8_rmsnorm): the
+    in-kernel norm of the fp32-tile path, the norm pass of the planes path
+    (long K walks, m > 64) and the CUDA-core path (k % 8 != 0). The
+    normalized values are those of accel_b200_rmsnorm, so the result equals
+    RmsNorm then the product bit for bit, and the checker's RmsNorm + MatMul
+    within tolerance."""
+    rng = np.random.default_rng(m + k + n)
+    xs = rng.standard_normal((m, ldx), dtype=np.float32) * 3
+    gamma = (rng.standard_normal(k, dtype=np.float32) * 0.5 + 1).astype(np.float32)
+    _, w, s = syn.int8_gemm(1, k, n, m * n)
+    x = np.ascontiguousarray(xs[:, :k])
+    normed = orc.rmsnorm(x, gamma, m, k, 1e-5)
+    want = orc.execute_matmul_q(normed, w, s, act="relu")
+    mag = np.abs(normed).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
+    xt, gt, wt, st = T(xs), T(gamma), T(w), T(s)
+    got = H(K.matmul_q8_rmsnorm(xt, gt, 1e-5, wt, st, epilogue=K.make_epilogue(act="relu")))
+    check_close(got, want, k, mag)
+    dev_normed = K.rmsnorm(xt[:, :k].contiguous(), gt, m, k, 1e-5)
+    two_step = H(K.matmul_q8(dev_normed, wt, st, epilogue=K.make_epilogue(act="relu")))
+    assert np.array_equal(got, two_step)
