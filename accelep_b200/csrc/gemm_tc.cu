@@ -103,6 +103,7 @@ struct TcArgs {
   float* c;
   int64_t ldc;
   int32_t* status;
+  int32_t vec_store;  // c and ldc allow 16-byte row stores
   Epilogue ep;
 };
 
@@ -261,7 +262,7 @@ __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int6
     for (int j = 0; j < 8; ++j) s[j] = 0.0;
     if (r < valid) {
       const float* in = a + (row0 + r) * lda + 8 * q;
-#pragma unroll 6
+#pragma unroll 9
       for (int64_t i0 = 0; i0 + 8 * q < dim; i0 += 32) {
         const float4 x0 = __ldg(reinterpret_cast<const float4*>(in + i0));
         const float4 x1 = __ldg(reinterpret_cast<const float4*>(in + i0 + 4));
@@ -494,48 +495,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     return;
   }
+  // Rank `rank` sums rows [rank * rpr, +rpr) of the tile over the cluster; a
+  // thread owns one group of four columns (tid % 32) in rows tid / 32, + 6, ...
+  const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
+  const int rpr = (static_cast<int>(rows) + splits - 1) / splits;
+  const int c4 = (tid & 31) * 4;
+  const int r_begin = rank * rpr + (tid >> 5);
+  const int r_end = min(static_cast<int>(rows), (rank + 1) * rpr);
+  constexpr int kMaxJ = (R / 2 + kThreads / 32 - 1) / (kThreads / 32);  // rows per thread (splits >= 2)
+  float sc[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
+  }
   ClusterSync();  // every partial tile (and ok flag) of the cluster is complete
   bool all_ok = true;
   for (int p = 0; p < splits; ++p) all_ok &= LoadPeerInt(&ok_s, static_cast<uint32_t>(p)) != 0;
-  if (all_ok) {
-    // The tile's rows * 32 groups of four columns are dealt out to the cluster
-    // in contiguous ranges; each group is summed over ranks 0, 1, ... in order.
-    const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
-    const int groups = static_cast<int>(rows) * (kBn / 4);
-    const int per = (groups + splits - 1) / splits;
-    const int g_end = min(groups, (rank + 1) * per);
-#pragma unroll 1
-    for (int idx = rank * per + tid; idx < g_end; idx += kThreads) {
-      const int r = idx >> 5, c4 = (idx & 31) * 4;
-      if (c4 >= cols) continue;
-      const float* src = tile + r * kBn + c4;
-      float4 part[8];
+  float4 sum[kMaxJ];
+  if (all_ok && c4 < cols) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (q < splits) part[q] = LoadPeer4(src, static_cast<uint32_t>(q));
-      float4 sum = part[0];
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int r = r_begin + j * (kThreads / 32);
+      if (r < r_end) {
+        // Summed over ranks 0, 1, ... in order: the result does not depend on
+        // which rank finished first.
+        const float* src = tile + r * kBn + c4;
+        float4 part[8];
 #pragma unroll
-      for (int q = 1; q < 8; ++q) {
-        if (q < splits) {
-          sum.x += part[q].x;
-          sum.y += part[q].y;
-          sum.z += part[q].z;
-          sum.w += part[q].w;
+        for (int q = 0; q < 8; ++q)
+          if (q < splits) part[q] = LoadPeer4(src, static_cast<uint32_t>(q));
+        float4 acc = part[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) {
+          if (q < splits) {
+            acc.x += part[q].x;
+            acc.y += part[q].y;
+            acc.z += part[q].z;
+            acc.w += part[q].w;
+          }
         }
+        sum[j] = acc;
       }
-      const float v[4] = {sum.x, sum.y, sum.z, sum.w};
-      const int64_t row = row0 + r;
+    }
+  }
+  // This CTA has read what it needs from its peers: arrive now, and wait for
+  // the peers' reads of this CTA's tile only before leaving.
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  if (all_ok && c4 < cols) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t col = n0 + c4 + j;
-        if (c4 + j < cols) {
-          const float sc = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
-          g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(v[j], sc), row, col);
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int r = r_begin + j * (kThreads / 32);
+      if (r < r_end) {
+        const int64_t row = row0 + r;
+        const float v[4] = {sum[j].x, sum[j].y, sum[j].z, sum[j].w};
+        float o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q);
+        float* dst = g.c + row * g.ldc + n0 + c4;
+        if (g.vec_store && c4 + 4 <= cols) {
+          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (c4 + q < cols) dst[q] = o[q];
         }
       }
     }
   }
-  ClusterSync();  // no CTA leaves while a peer may still read its tile
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // peers are done with this tile
 }
 
 // fp32 [m, k] (row stride lda) -> three bf16 planes [3][m][k] (Split3). With
@@ -773,6 +800,7 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   g.c = c;
   g.ldc = ldc;
   g.status = status;
+  g.vec_store = (reinterpret_cast<uintptr_t>(c) % 16 == 0 && ldc % 4 == 0) ? 1 : 0;
   g.ep = ep;
   if (p.mode == kAPlanes) {
     switch (p.r) {
