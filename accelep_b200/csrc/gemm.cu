@@ -349,14 +349,29 @@ int LaunchRmsNormRows(const float* x, int64_t ldx, const float* w, float* y, int
 int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
                       cudaStream_t stream);
 
+// GEMV for m <= 8 (gemv.cu).
+bool GemvEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m,
+                  int64_t k, int64_t n);
+int RunGemv(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c,
+            int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, cudaStream_t stream);
+
 namespace {
-std::atomic<int> g_q8_path{0};  // 0: by shape, 1: CUDA cores, 2: tensor cores where eligible
+// 0: by shape (GEMV for m <= 8, tensor cores above), 1: CUDA cores,
+// 2: tensor cores where eligible, 3: GEMV where eligible.
+std::atomic<int> g_q8_path{0};
 
 bool UseTc(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
            int64_t n) {
   const int path = g_q8_path.load(std::memory_order_relaxed);
-  if (path == 1) return false;
+  if (path == 1 || path == 3) return false;
   return TcEligible(a, lda, w, axis, zero, m, k, n);
+}
+
+bool UseGemv(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
+             int64_t n) {
+  const int path = g_q8_path.load(std::memory_order_relaxed);
+  if (path == 1 || path == 2) return false;
+  return GemvEligible(a, lda, w, axis, zero, m, k, n);
 }
 }  // namespace
 }  // namespace accel_b200
@@ -383,7 +398,9 @@ ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64
 }
 
 ACCEL_B200_API int accel_b200_set_q8_path(int32_t path) {
-  if (path < 0 || path > 2) return SetError(ACCEL_B200_EINVAL, "set_q8_path: 0 (by shape), 1 (CUDA cores) or 2");
+  if (path < 0 || path > 3) {
+    return SetError(ACCEL_B200_EINVAL, "set_q8_path: 0 (by shape), 1 (CUDA cores), 2 (tensor cores), 3 (GEMV)");
+  }
   g_q8_path.store(path, std::memory_order_relaxed);
   return ClearError();
 }
@@ -407,6 +424,9 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
     return SetError(ACCEL_B200_EINVAL, "quantized MatMul is missing an operand");
   }
   const int8_t* w = b->q + b->offset;
+  if (UseGemv(a, lda, w, b->axis, b->zero, m, k, n)) {
+    return RunGemv(a, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, AsStream(stream));
+  }
   if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
     return RunTc(a, nullptr, lda, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace,
                  workspace_bytes, nullptr, AsStream(stream));

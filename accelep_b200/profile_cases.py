@@ -1,6 +1,6 @@
 """Times single kernels of the backend on fixed cases, for profiling.
 
-    python -m accelep_b200.profile_cases gemm [--path tc|simt] [--shapes decode|prefill|c5|all]
+    python -m accelep_b200.profile_cases gemm [--path auto|tc|gemv|simt] [--shapes decode|prefill|c5|all]
     python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280] [--kind fused|split|prefill]
     python -m accelep_b200.profile_cases step [--reps 3]
     python -m accelep_b200.profile_cases list
@@ -177,7 +177,7 @@ def attention_case(batch, length, reps, kind="fused", context=2048, heads=9, kv_
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attention", "step", "list"])
-    ap.add_argument("--path", default="tc", choices=["tc", "simt"])
+    ap.add_argument("--path", default="auto", choices=["auto", "tc", "gemv", "simt"])
     ap.add_argument("--shapes", default="decode", choices=["decode", "prefill", "c5", "all"])
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--len", type=int, default=1280)
@@ -190,7 +190,7 @@ def main():
         return
     torch.cuda.set_device(0)
     if args.what == "gemm":
-        K.set_q8_path(1 if args.path == "simt" else 0)
+        K.set_q8_path({"auto": 0, "simt": 1, "tc": 2, "gemv": 3}[args.path])
         groups = list(GEMM_SHAPES) if args.shapes == "all" else [args.shapes]
         for group in groups:
             for name, m, k, n in GEMM_SHAPES[group]:

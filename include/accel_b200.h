@@ -157,9 +157,10 @@ typedef struct accel_b200_epilogue {
 ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64_t n);
 
 /* Which kernel accel_b200_matmul_q8 uses, process-wide: 0 by shape (the
-   default: the tcgen05 tensor-core kernel for per-column or single scales
-   without zero points and 16-byte aligned rows, CUDA cores otherwise), 1
-   CUDA cores only, 2 the same as 0. For comparisons and tests. */
+   default: for per-column or single scales without zero points and 16-byte
+   aligned rows, the int8 GEMV for m <= 8 and the tcgen05 tensor-core kernel
+   above; CUDA cores otherwise), 1 CUDA cores only, 2 the tensor-core kernel
+   where eligible, 3 the GEMV where eligible. For comparisons and tests. */
 ACCEL_B200_API int accel_b200_set_q8_path(int32_t path);
 
 /* src/sim_device.cc:541-602 (MatMulQuantized with a right-hand plane) and

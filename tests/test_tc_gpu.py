@@ -31,8 +31,10 @@ def check_close(got, want, k, scale_mag):
 
 
 @pytest.fixture(autouse=True)
-def by_shape():
-    K.set_q8_path(0)
+def tensor_cores():
+    """Every product in this file on the tensor-core kernel where eligible
+    (the default path sends m <= 16 to the GEMV)."""
+    K.set_q8_path(2)
     yield
     K.set_q8_path(0)
 
@@ -93,7 +95,7 @@ def test_silu_product_matches_checker(lib, cuda, orc, m, inter, n):
     act = orc.silu_mul(np.ascontiguousarray(gu[:, :inter]), np.ascontiguousarray(gu[:, inter:]))
     want = orc.execute_matmul_q(act, w, s, residual=res)
     mag = np.abs(act).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
-    for path in (0, 1):
+    for path in (2, 1):
         K.set_q8_path(path)
         ep = K.make_epilogue(residual=T(res))
         got = H(K.matmul_q8_silu(T(gu), T(w), T(s), epilogue=ep))
