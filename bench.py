@@ -262,6 +262,59 @@ def products_roofline(torch, stream, reps=3):
     return per_launch / sec / 1e9, sec, per_launch
 
 
+def gemv_roofline(torch, reps=20):
+    """The C5 dequant GEMV at M=1, K=N=16384 (BASELINE's second metric:
+    dequant-GEMV GB/s against HBM), timed as profile_cases times it."""
+    from accelep_b200 import profile_cases as PC
+
+    row = PC.gemm_case("c5_m1_k16384", 1, 16384, 16384, reps)
+    torch.cuda.empty_cache()
+    return row
+
+
+def c5_sharded(torch, dist, world, rank, reps=10):
+    """C5 sweep points with W N-sharded across the ranks and Y all-gathered
+    over NCCL (accelep_b200/sharded.py): every rank's local product plus the
+    gather, timed with CUDA events, max over ranks. Weights are seeded
+    synthetic int8 with per-column scales (each rank draws its own block)."""
+    from accelep_b200 import sharded
+
+    out = []
+    for m, kn in ((1, 16384), (2048, 8192)):
+        k = n = kn
+        gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+        nr = n // world
+        copies = 2 if m == 1 else 1
+        layers = []
+        for _ in range(copies):
+            w = torch.randint(-127, 128, (k, nr), dtype=torch.int8, device="cuda", generator=gen)
+            sc = torch.rand(nr, device="cuda", generator=gen) * 9e-3 + 1e-3
+            layers.append(sharded.ShardedQ8Linear(w, sc))
+        x = torch.randn(m, k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7))
+        for i in range(3):
+            layers[i % copies](x)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(reps):
+            y = layers[i % copies](x)
+        end.record()
+        end.synchronize()
+        sec = start.elapsed_time(end) / 1000.0 / reps
+        t = torch.tensor([sec], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t[0])
+        assert y.shape == (m, n)
+        out.append({"m": m, "k": k, "n": n, "us_per_call": sec * 1e6,
+                    "weight_gbs_all_ranks": k * n / sec / 1e9, "tflops_all_ranks": 2.0 * m * k * n / sec / 1e12})
+        del layers, x, y
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -289,6 +342,12 @@ def run_b200(args):
 
     def step():
         return model.generate_batch(prompts, new)
+
+    # C5 first, on a cool GPU, with its own clock record.
+    c5_clocks = ClockSampler(local)
+    c5_clocks.start()
+    sharded_rows = c5_sharded(torch, dist, world, rank)
+    c5_clk = c5_clocks.stop()
 
     for _ in range(max(3, args.warmup)):
         out = step()
@@ -327,6 +386,7 @@ def run_b200(args):
         peak, peak_kind = hbm_peak()
         achieved, sec, nbytes = attention_roofline(torch, stream)
         p_achieved, p_sec, p_bytes = products_roofline(torch, stream)
+        gemv = gemv_roofline(torch)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cores = 1
@@ -354,6 +414,15 @@ def run_b200(args):
                                        "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                                        "frac": achieved / peak, "traffic": ATTENTION_TRAFFIC,
                                        "bytes_per_launch": nbytes, "us_per_launch": sec * 1e6},
+                "dequant_gemv": {"config": "C5 sweep point M=1, K=N=16384: fp32 X, int8 W [K,N], per-column fp32 "
+                                           "scales; accel_b200_matmul_q8 (GEMV path), graph-replayed, 2 weight "
+                                           "copies rotated (512 MB > L2)",
+                                 "us_per_launch": gemv["us"], "achieved": gemv["gbs"], "peak": peak,
+                                 "peak_kind": peak_kind, "unit": "GB/s", "frac": gemv["gbs"] / peak,
+                                 "bytes_per_launch": 16384 * 16384 + 4 * 16384 * 3},
+                "c5_sharded": {"what": "int8 GEMM sweep points with W N-sharded over the ranks and Y all-gathered "
+                                       "(NCCL all_gather_into_tensor); one call = local product + gather; max over "
+                                       "ranks", "ranks": world, "points": sharded_rows, "clocks": c5_clk},
                 "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line), flush=True)
     model.close()
