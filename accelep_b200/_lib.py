@@ -61,6 +61,9 @@ SIGNATURES = {
     "accel_b200_matmul_q8_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_set_q8_path": (c_int, [c_i32]),
     "accel_b200_matmul_q8": (c_int, [c_vp, c_i64, P_plane, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
+    "accel_b200_matmul_q8_peers": (c_int, [c_vp, c_i64, P_plane, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i32, P_ep,
+                                           c_vp, c_sz, c_vp]),
+    "accel_b200_peer_barrier": (c_int, [c_vp, c_vp, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp]),
     "accel_b200_matmul_q8_silu_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_q8_silu": (c_int, [c_vp, c_i64, c_i64, P_plane, c_vp, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz,
                                           c_vp]),

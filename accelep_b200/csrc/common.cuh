@@ -98,6 +98,24 @@ __device__ __forceinline__ float GeluExact(float v) {
   return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.f, e));
 }
 
+// Output copies on other GPUs: the same element is also stored to each peer
+// buffer at the same offset (peer memory mapped into this process, written
+// over NVLink). Used to fuse an all-gather into a product's epilogue.
+constexpr int kMaxPeers = 7;
+struct PeerOut {
+  float* c[kMaxPeers];
+  int32_t n;
+};
+
+// Element `offset` (from the output's base) to every peer copy.
+__device__ __forceinline__ void StorePeers(const PeerOut& peers, int64_t offset, float v) {
+  for (int i = 0; i < peers.n; ++i) peers.c[i][offset] = v;
+}
+
+__device__ __forceinline__ void StorePeers4(const PeerOut& peers, int64_t offset, float4 v) {
+  for (int i = 0; i < peers.n; ++i) *reinterpret_cast<float4*>(peers.c[i] + offset) = v;
+}
+
 // Epilogue of a product (include/accel_b200.h, accel_b200_epilogue), applied to
 // one output element: act(alpha * acc + beta * bias) + residual, each step a
 // rounded float operation as in sim_device.cc:227-241 and runtime.cc:336-344.

@@ -343,7 +343,8 @@ bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, cons
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n);
 int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
           const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
-          const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream);
+          const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream,
+          const PeerOut* peers);
 int LaunchRmsNormRows(const float* x, int64_t ldx, const float* w, float* y, int64_t ldy, int64_t rows, int64_t dim,
                       float eps, int64_t row_offset, cudaStream_t stream);
 int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
@@ -353,7 +354,8 @@ int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo,
 bool GemvEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m,
                   int64_t k, int64_t n);
 int RunGemv(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c,
-            int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, cudaStream_t stream);
+            int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, cudaStream_t stream,
+            const PeerOut* peers);
 
 namespace {
 // 0: by shape (GEMV for m <= 8, tensor cores above), 1: CUDA cores,
@@ -372,6 +374,51 @@ bool UseGemv(const float* a, int64_t lda, const int8_t* w, int32_t axis, const i
   const int path = g_q8_path.load(std::memory_order_relaxed);
   if (path == 1 || path == 2) return false;
   return GemvEligible(a, lda, w, axis, zero, m, k, n);
+}
+}  // namespace
+}  // namespace accel_b200
+
+namespace accel_b200 {
+namespace {
+int MatMulQ8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m, int64_t k,
+             int64_t n, const accel_b200_epilogue* ep, void* workspace, size_t workspace_bytes, void* stream,
+             const PeerOut* peers) {
+  if (m < 0 || k < 0 || n < 0 || b == nullptr) return SetError(ACCEL_B200_EINVAL, "quantized MatMul is out of range");
+  if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
+  GemmArgs g{};
+  if (!ToEpilogue(ep, &g.ep)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
+  if (m == 0 || n == 0) return ClearError();
+  if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
+  const bool with_peers = peers != nullptr && peers->n > 0;
+  if (k == 0 && !with_peers) return EmptySum(c, ldc, m, n, g.ep, AsStream(stream));
+  if (a == nullptr || lda < k || b->q == nullptr || b->scale == nullptr) {
+    return SetError(ACCEL_B200_EINVAL, "quantized MatMul is missing an operand");
+  }
+  const int8_t* w = b->q + b->offset;
+  if (UseGemv(a, lda, w, b->axis, b->zero, m, k, n)) {
+    return RunGemv(a, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, AsStream(stream), peers);
+  }
+  if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
+    return RunTc(a, nullptr, lda, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace,
+                 workspace_bytes, nullptr, AsStream(stream), peers);
+  }
+  if (with_peers) {
+    return SetError(ACCEL_B200_EINVAL,
+                    "matmul_q8_peers: needs the GEMV or tensor-core path (per-column or single scale, no zero "
+                    "points, 16-byte aligned rows, k % 8 == 0 and n % 16 == 0 above m = 8)");
+  }
+  g.a = a;
+  g.lda = lda;
+  g.w = w;
+  g.scale = b->scale;
+  g.zero = b->zero;
+  g.axis = b->axis;
+  g.c = c;
+  g.ldc = ldc;
+  g.m = m;
+  g.k = k;
+  g.n = n;
+  return RunGemm<int8_t>(g, AsStream(stream), workspace, workspace_bytes);
 }
 }  // namespace
 }  // namespace accel_b200
@@ -409,40 +456,28 @@ ACCEL_B200_API size_t accel_b200_matmul_f32_workspace(int64_t m, int64_t k, int6
   return WorkspaceFor(false, m, k, n);
 }
 
+
 ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c,
                                         int64_t ldc, int64_t m, int64_t k, int64_t n,
                                         const accel_b200_epilogue* ep, void* workspace, size_t workspace_bytes,
                                         void* stream) {
-  if (m < 0 || k < 0 || n < 0 || b == nullptr) return SetError(ACCEL_B200_EINVAL, "quantized MatMul is out of range");
-  if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
-  GemmArgs g{};
-  if (!ToEpilogue(ep, &g.ep)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
-  if (m == 0 || n == 0) return ClearError();
-  if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
-  if (k == 0) return EmptySum(c, ldc, m, n, g.ep, AsStream(stream));
-  if (a == nullptr || lda < k || b->q == nullptr || b->scale == nullptr) {
-    return SetError(ACCEL_B200_EINVAL, "quantized MatMul is missing an operand");
+  return MatMulQ8(a, lda, b, c, ldc, m, k, n, ep, workspace, workspace_bytes, stream, nullptr);
+}
+
+ACCEL_B200_API int accel_b200_matmul_q8_peers(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c,
+                                              int64_t ldc, int64_t m, int64_t k, int64_t n, float* const* peers,
+                                              int32_t n_peers, const accel_b200_epilogue* ep, void* workspace,
+                                              size_t workspace_bytes, void* stream) {
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peers == nullptr)) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_peers: 0 to 7 peer outputs");
   }
-  const int8_t* w = b->q + b->offset;
-  if (UseGemv(a, lda, w, b->axis, b->zero, m, k, n)) {
-    return RunGemv(a, lda, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, AsStream(stream));
+  PeerOut p{};
+  p.n = n_peers;
+  for (int i = 0; i < n_peers; ++i) {
+    if (peers[i] == nullptr) return SetError(ACCEL_B200_EINVAL, "matmul_q8_peers: null peer output");
+    p.c[i] = peers[i];
   }
-  if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
-    return RunTc(a, nullptr, lda, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace,
-                 workspace_bytes, nullptr, AsStream(stream));
-  }
-  g.a = a;
-  g.lda = lda;
-  g.w = w;
-  g.scale = b->scale;
-  g.zero = b->zero;
-  g.axis = b->axis;
-  g.c = c;
-  g.ldc = ldc;
-  g.m = m;
-  g.k = k;
-  g.n = n;
-  return RunGemm<int8_t>(g, AsStream(stream), workspace, workspace_bytes);
+  return MatMulQ8(a, lda, b, c, ldc, m, k, n, ep, workspace, workspace_bytes, stream, &p);
 }
 
 ACCEL_B200_API size_t accel_b200_matmul_q8_silu_workspace(int64_t m, int64_t inter, int64_t n) {
@@ -475,7 +510,7 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
   if (inter % 4 == 0 && UseTc(gate_up, ld, w, b->axis, b->zero, m, inter, n) &&
       reinterpret_cast<uintptr_t>(up) % 16 == 0) {
     return RunTc(gate_up, up, ld, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, inter, n, e, workspace,
-                 workspace_bytes, nullptr, AsStream(stream));
+                 workspace_bytes, nullptr, AsStream(stream), nullptr);
   }
   // CUDA cores: SiluMul rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * inter * sizeof(float);
@@ -515,7 +550,7 @@ ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, con
   const int8_t* w = b->q + b->offset;
   if (UseTc(x, ldx, w, b->axis, b->zero, m, k, n) && reinterpret_cast<uintptr_t>(gamma) % 16 == 0) {
     return RunTc(x, nullptr, ldx, gamma, eps, w, b->scale, b->axis < 0, c, ldc, m, k, n, e, workspace,
-                 workspace_bytes, nullptr, AsStream(stream));
+                 workspace_bytes, nullptr, AsStream(stream), nullptr);
   }
   // CUDA cores: RmsNorm rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * k * sizeof(float);

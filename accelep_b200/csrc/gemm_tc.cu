@@ -105,6 +105,7 @@ struct TcArgs {
   int32_t* status;
   int32_t vec_store;  // c and ldc allow 16-byte row stores
   Epilogue ep;
+  PeerOut peers;  // copies of C on other GPUs (n = 0: none)
 };
 
 __device__ __forceinline__ void TmaLoad2D(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
@@ -490,9 +491,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 4
       for (int64_t r = 0; r < rows; ++r) {
         const int64_t row = row0 + r;
-        g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
+        const float o = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
+        g.c[row * g.ldc + col] = o;
+        StorePeers(g.peers, row * g.ldc + col, o);
       }
     }
+    if (g.peers.n > 0) __threadfence_system();
     return;
   }
   // Rank `rank` sums rows [rank * rpr, +rpr) of the tile over the cluster; a
@@ -551,17 +555,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         float o[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q);
-        float* dst = g.c + row * g.ldc + n0 + c4;
+        const int64_t off = row * g.ldc + n0 + c4;
+        float* dst = g.c + off;
         if (g.vec_store && c4 + 4 <= cols) {
           *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+          StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
         } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (c4 + q < cols) dst[q] = o[q];
+          for (int q = 0; q < 4; ++q) {
+            if (c4 + q < cols) {
+              dst[q] = o[q];
+              StorePeers(g.peers, off + q, o[q]);
+            }
+          }
         }
       }
     }
   }
+  if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // peers are done with this tile
 }
 
@@ -743,7 +754,8 @@ size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
 // for a (and up).
 int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
           const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
-          const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream) {
+          const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream,
+          const PeerOut* peers) {
   const TcPlan p = MakeTcPlan(m, k, n, up != nullptr, gamma != nullptr);
   if (p.planes_bytes > 0 && (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes)) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
@@ -802,6 +814,10 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   g.status = status;
   g.vec_store = (reinterpret_cast<uintptr_t>(c) % 16 == 0 && ldc % 4 == 0) ? 1 : 0;
   g.ep = ep;
+  g.peers = peers != nullptr ? *peers : PeerOut{};
+  for (int i = 0; i < g.peers.n; ++i) {
+    if (reinterpret_cast<uintptr_t>(g.peers.c[i]) % 16 != 0) g.vec_store = 0;
+  }
   if (p.mode == kAPlanes) {
     switch (p.r) {
       case 32: return LaunchTcStages<32, kAPlanes>(tw, tx, tu, g, p, stream);

@@ -45,6 +45,7 @@ struct GemvArgs {
   int64_t k_per_slice;  // multiple of kGvUnroll
   int32_t vec_store;
   Epilogue ep;
+  PeerOut peers;  // copies of C on other GPUs (n = 0: none)
 };
 
 template <int CPL>
@@ -211,15 +212,22 @@ __global__ void __launch_bounds__(kGvThreads) Q8GemvKernel(GemvArgs g) {
       const float scq = g.scalar_scale ? __ldg(g.scale) : (col + q < g.n ? __ldg(g.scale + col + q) : 0.f);
       o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], scq), row, col + q);
     }
-    float* dst = g.c + row * g.ldc + col;
+    const int64_t off = row * g.ldc + col;
+    float* dst = g.c + off;
     if (g.vec_store && col + 4 <= g.n) {
       *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+      StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
     } else {
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (col + q < g.n) dst[q] = o[q];
+      for (int q = 0; q < 4; ++q) {
+        if (col + q < g.n) {
+          dst[q] = o[q];
+          StorePeers(g.peers, off + q, o[q]);
+        }
+      }
     }
   }
+  if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes
   if (splits > 1) ClusterSync();  // no CTA leaves while a peer may still read its sum
 }
 
@@ -276,7 +284,8 @@ bool GemvEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, co
 }
 
 int RunGemv(const float* a, int64_t lda, const int8_t* w, const float* scale, bool scalar_scale, float* c,
-            int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, cudaStream_t stream) {
+            int64_t ldc, int64_t m, int64_t k, int64_t n, const Epilogue& ep, cudaStream_t stream,
+            const PeerOut* peers) {
   const GvPlan p = MakeGvPlan(m, k, n);
   GemvArgs g{};
   g.a = a;
@@ -292,6 +301,10 @@ int RunGemv(const float* a, int64_t lda, const int8_t* w, const float* scale, bo
   g.k_per_slice = p.k_per_slice;
   g.vec_store = (reinterpret_cast<uintptr_t>(c) % 16 == 0 && ldc % 4 == 0) ? 1 : 0;
   g.ep = ep;
+  g.peers = peers != nullptr ? *peers : PeerOut{};
+  for (int i = 0; i < g.peers.n; ++i) {
+    if (reinterpret_cast<uintptr_t>(g.peers.c[i]) % 16 != 0) g.vec_store = 0;
+  }
   switch (p.mt * 100 + p.cpl) {
     case 116: return LaunchGv<1, 16>(g, p, stream);
     case 108: return LaunchGv<1, 8>(g, p, stream);

@@ -8,9 +8,23 @@ GPUs) assembles Y on every rank. There is no reduction: each output column is
 computed by exactly one rank, so Y is bit-identical to the unsharded
 product's columns computed by the same kernel.
 
-The local product is a parameter so that the gather logic can run on CPU
+Two ways to assemble Y:
+  * mode "nccl": the local block goes to a buffer and NCCL's all-gather
+    (all_gather_into_tensor) collects the blocks; a transpose copy makes Y.
+  * mode "fused": Y lives in symmetric memory (every rank's Y mapped into every
+    process); the product kernel itself stores each output element of its
+    block into every rank's Y (accel_b200_matmul_q8_peers, peer stores over
+    NVLink from the epilogue), then the ranks meet at a barrier over peer
+    memory (accel_b200_peer_barrier, bounded wait). No copy, no separate
+    collective; two Y buffers alternate so that a rank one call ahead never
+    overwrites a Y a peer may still read (so a captured CUDA graph must hold
+    an even number of calls).
+
+The local product is a parameter so that the nccl gather logic can run on CPU
 ranks (gloo) with a CPU product in tests.
 """
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -38,7 +52,10 @@ class ShardedQ8Linear:
     (x, w, scale, out) -> out, the local product (default: the CUDA kernels).
     """
 
-    def __init__(self, w_shard, scale_shard, group=None, product=None):
+    def __init__(self, w_shard, scale_shard, group=None, product=None, mode="nccl"):
+        if mode not in ("nccl", "fused"):
+            raise ValueError("mode is 'nccl' or 'fused'")
+        self.mode = mode
         self.group = group
         initialized = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if initialized else 1
@@ -48,6 +65,8 @@ class ShardedQ8Linear:
         self.nr = w_shard.shape[1]
         self.product = product or _gpu_product
         self._bufs = {}
+        self._fused = {}
+        self.status = None
 
     def _buffers(self, m, device):
         key = (m, str(device))
@@ -57,8 +76,60 @@ class ShardedQ8Linear:
             self._bufs[key] = (local, gathered)
         return self._bufs[key]
 
+    def _fused_state(self, m, device):
+        key = (m, str(device))
+        if key in self._fused:
+            return self._fused[key]
+        import torch.distributed._symmetric_memory as symm_mem
+
+        group = self.group if self.group is not None else dist.group.WORLD
+        n = self.world * self.nr
+        ys = []
+        for _ in range(2):
+            y = symm_mem.empty(m, n, dtype=torch.float32, device=device)
+            hdl = symm_mem.rendezvous(y, group)
+            # This rank's column block in every peer's Y.
+            peers = [hdl.buffer_ptrs[p] + self.rank * self.nr * 4 for p in range(self.world) if p != self.rank]
+            ys.append((y, hdl, (ctypes.c_void_p * 7)(*peers), len(peers)))
+        flags = symm_mem.empty(8, dtype=torch.int32, device=device)
+        flags.zero_()
+        fh = symm_mem.rendezvous(flags, group)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before any signal
+        flag_ptrs = (ctypes.c_void_p * 8)(*[fh.buffer_ptrs[p] for p in range(self.world)])
+        if self.status is None:
+            self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        state = {"ys": ys, "next": 0, "flags": flags, "fh": fh, "flag_ptrs": flag_ptrs, "epoch": epoch}
+        self._fused[key] = state
+        return state
+
+    def _forward_fused(self, x):
+        from . import kernels as K
+        from ._lib import Q8Plane, check, load
+
+        lib = load()
+        m, k = x.shape
+        st = self._fused_state(m, x.device)
+        y, _hdl, peers, n_peers = st["ys"][st["next"]]
+        st["next"] ^= 1
+        n = self.world * self.nr
+        plane = Q8Plane(self.w.data_ptr(), self.scale.data_ptr(), 0, 0, 1)
+        need = lib.accel_b200_matmul_q8_workspace(m, k, self.nr)
+        ws = K._workspace(x.device, need)
+        stream = K._s()
+        local = y.data_ptr() + self.rank * self.nr * 4
+        check(lib.accel_b200_matmul_q8_peers(ctypes.c_void_p(x.data_ptr()), x.stride(0), ctypes.byref(plane),
+                                             ctypes.c_void_p(local), n, m, k, self.nr, peers, n_peers, None,
+                                             K._p(ws), 0 if ws is None else ws.numel(), stream))
+        check(lib.accel_b200_peer_barrier(st["flag_ptrs"], ctypes.c_void_p(st["flags"].data_ptr()), self.rank,
+                                          self.world, K._p(st["epoch"]), 0, K._p(self.status), stream))
+        return y
+
     def forward(self, x):
         """Y [M, N] on every rank."""
+        if self.mode == "fused" and self.world > 1:
+            return self._forward_fused(x)
         m = x.shape[0]
         local, gathered = self._buffers(m, x.device)
         self.product(x, self.w, self.scale, local)

@@ -273,44 +273,63 @@ def gemv_roofline(torch, reps=20):
 
 
 def c5_sharded(torch, dist, world, rank, reps=10):
-    """C5 sweep points with W N-sharded across the ranks and Y all-gathered
-    over NCCL (accelep_b200/sharded.py): every rank's local product plus the
-    gather, timed with CUDA events, max over ranks. Weights are seeded
+    """C5 sweep points with W N-sharded across the ranks
+    (accelep_b200/sharded.py), timed with CUDA events, max over ranks. At N > 1
+    two ways to assemble Y: "nccl" (local product, NCCL all-gather, transpose
+    copy) and "fused" (the product kernel stores its block into every rank's
+    Y over NVLink, then a barrier over peer memory). Weights are seeded
     synthetic int8 with per-column scales (each rank draws its own block)."""
     from accelep_b200 import sharded
 
     out = []
+    modes = ("nccl", "fused") if world > 1 else ("local",)
     for m, kn in ((1, 16384), (2048, 8192)):
         k = n = kn
         gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
         nr = n // world
         copies = 2 if m == 1 else 1
-        layers = []
+        weights = []
         for _ in range(copies):
             w = torch.randint(-127, 128, (k, nr), dtype=torch.int8, device="cuda", generator=gen)
             sc = torch.rand(nr, device="cuda", generator=gen) * 9e-3 + 1e-3
-            layers.append(sharded.ShardedQ8Linear(w, sc))
+            weights.append((w, sc))
         x = torch.randn(m, k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7))
-        for i in range(3):
-            layers[i % copies](x)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for i in range(reps):
-            y = layers[i % copies](x)
-        end.record()
-        end.synchronize()
-        sec = start.elapsed_time(end) / 1000.0 / reps
-        t = torch.tensor([sec], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        sec = float(t[0])
-        assert y.shape == (m, n)
-        out.append({"m": m, "k": k, "n": n, "us_per_call": sec * 1e6,
-                    "weight_gbs_all_ranks": k * n / sec / 1e9, "tflops_all_ranks": 2.0 * m * k * n / sec / 1e12})
-        del layers, x, y
+        for mode in modes:
+            layers = [sharded.ShardedQ8Linear(w, sc, mode="nccl" if mode == "local" else mode) for w, sc in weights]
+            stream = torch.cuda.Stream()
+            with torch.cuda.stream(stream):
+                for i in range(4):
+                    layers[i % copies](x)
+                torch.cuda.synchronize()
+                # `reps` calls in one CUDA graph (host launch cost out of the
+                # per-call time; an even count keeps the fused mode's buffer
+                # alternation aligned across replays).
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for i in range(reps):
+                        y = layers[i % copies](x)
+                graph.replay()
+                torch.cuda.synchronize()
+                if world > 1:
+                    dist.barrier()
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                graph.replay()
+                end.record(stream)
+                end.synchronize()
+                del graph
+            sec = start.elapsed_time(end) / 1000.0 / reps
+            t = torch.tensor([sec], dtype=torch.float64, device="cuda")
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sec = float(t[0])
+            assert y.shape == (m, n)
+            bad = any(int(l.status.item()) != 0 for l in layers if l.status is not None)
+            out.append({"mode": mode, "m": m, "k": k, "n": n, "us_per_call": sec * 1e6,
+                        "weight_gbs_all_ranks": k * n / sec / 1e9,
+                        "tflops_all_ranks": 2.0 * m * k * n / sec / 1e12, "barrier_timeout": bad})
+            del layers, y
+        del weights, x
         torch.cuda.empty_cache()
     return out
 
@@ -420,9 +439,11 @@ def run_b200(args):
                                  "us_per_launch": gemv["us"], "achieved": gemv["gbs"], "peak": peak,
                                  "peak_kind": peak_kind, "unit": "GB/s", "frac": gemv["gbs"] / peak,
                                  "bytes_per_launch": 16384 * 16384 + 4 * 16384 * 3},
-                "c5_sharded": {"what": "int8 GEMM sweep points with W N-sharded over the ranks and Y all-gathered "
-                                       "(NCCL all_gather_into_tensor); one call = local product + gather; max over "
-                                       "ranks", "ranks": world, "points": sharded_rows, "clocks": c5_clk},
+                "c5_sharded": {"what": "int8 GEMM sweep points with W N-sharded over the ranks; one call = local "
+                                       "product + assembly of Y on every rank (nccl: all_gather_into_tensor + "
+                                       "transpose; fused: peer stores from the product epilogue + peer-memory "
+                                       "barrier); max over ranks", "ranks": world, "points": sharded_rows,
+                               "clocks": c5_clk},
                 "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line), flush=True)
     model.close()

@@ -175,6 +175,39 @@ ACCEL_B200_API int accel_b200_matmul_q8(const float* a, int64_t lda, const accel
                                         const accel_b200_epilogue* ep, void* workspace, size_t workspace_bytes,
                                         void* stream);
 
+/* accel_b200_matmul_q8 that also stores every output element to each of
+   `n_peers` (<= 7) peer buffers at the same offset from the peer's base as
+   from `c`: device memory of other GPUs mapped into this process (symmetric
+   memory), written over NVLink from the product's epilogue. No reference
+   counterpart: the reference runs one device. It fuses the all-gather of the
+   N-sharded C5 product into the product: rank r passes c = Y + r * Nr (its
+   column block of a row-major Y [m, N], ldc = N) and the same column block of
+   every peer's Y. Only the GEMV and tensor-core paths take peers (per-column
+   or single scale, no zero points, 16-byte aligned rows); the caller
+   synchronizes the ranks (all stores of a launch are visible system-wide when
+   it completes). */
+ACCEL_B200_API int accel_b200_matmul_q8_peers(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c,
+                                              int64_t ldc, int64_t m, int64_t k, int64_t n, float* const* peers,
+                                              int32_t n_peers, const accel_b200_epilogue* ep, void* workspace,
+                                              size_t workspace_bytes, void* stream);
+
+/* Barrier of `world` (<= 8) ranks over peer memory, for the fused product +
+   all-gather above. No reference counterpart. peer_flags[p] is rank p's array
+   of `world` int32 flags (symmetric memory mapped into this process;
+   peer_flags[rank] may be NULL) and my_flags this rank's own array, all zero
+   before the first call; *epoch_counter is a device int32 of this rank,
+   zero before the first call, that the kernel advances by one per call (so a
+   captured launch replays correctly). Rank `rank` stores the new epoch into
+   slot `rank` of every peer's array and waits until every peer's slot in its
+   own array holds at least that epoch. The wait is bounded by limit_cycles SM
+   clock cycles (<= 0: about one second); a peer that does not arrive in time
+   ORs ACCEL_B200_STATUS_COPY_TIMEOUT into *status (device int, may be NULL)
+   and the call returns. Run one rank per GPU, every rank calling equally
+   often. */
+ACCEL_B200_API int accel_b200_peer_barrier(int32_t* const* peer_flags, int32_t* my_flags, int32_t rank, int32_t world,
+                                           int32_t* epoch_counter, int64_t limit_cycles, int32_t* status,
+                                           void* stream);
+
 /* c[m, n] = epilogue(SiluMul(gate_up) @ dequant(b)) for fused gate|up rows:
    row r of the product's A is silu(g) * u with g = gate_up[r * ld + i] and
    u = gate_up[r * ld + inter + i], i < inter (src/sim_silu.cc:8-13 followed by

@@ -34,3 +34,29 @@ def test_argument_errors_do_not_launch(lib, cuda):
         check(lib.accel_b200_matmul(None, None, None, -1, 1, 1, None))
     assert "out of range" in lib.accel_b200_last_error().decode()
     np.testing.assert_equal(int(lib.accel_b200_launch_count()) >= 0, True)
+
+
+def test_peer_barrier_times_out_without_a_peer(lib, cuda):
+    """The rank barrier of the fused all-gather waits for a peer that never
+    signals (rank 1 of 2 does not exist): the bounded wait runs out (about a
+    millisecond here), sets the timeout bit and returns; the context stays
+    usable. Rank 1's flag array is a scratch buffer on this GPU."""
+    import ctypes
+
+    mine = torch.zeros(2, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(2, dtype=torch.int32, device="cuda")
+    flags = (ctypes.c_void_p * 8)(mine.data_ptr(), scratch.data_ptr())
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    check(lib.accel_b200_peer_barrier(flags, K._p(mine), 0, 2, K._p(epoch), 2_000_000, K._p(status), K._s()))
+    torch.cuda.synchronize()
+    assert int(status.item()) & 2
+    assert scratch.cpu().tolist() == [1, 0]  # this rank's signal (epoch 1) landed in the peer's slot 0
+    assert int(epoch.item()) == 1
+    # Once the peer's signal is there, the next barrier (epoch 2) passes without a timeout.
+    mine[1] = 2
+    status.zero_()
+    check(lib.accel_b200_peer_barrier(flags, K._p(mine), 0, 2, K._p(epoch), 2_000_000, K._p(status), K._s()))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert scratch.cpu().tolist() == [2, 0] and int(epoch.item()) == 2
