@@ -3,6 +3,7 @@
     python -m accelep_b200.profile_cases gemm [--path auto|tc|gemv|simt] [--shapes decode|prefill|c5|all]
     python -m accelep_b200.profile_cases attention [--batch 32] [--len 1280] [--kind fused|split|prefill]
     python -m accelep_b200.profile_cases step [--reps 3]
+    python -m accelep_b200.profile_cases mlp [--reps 20]
     python -m accelep_b200.profile_cases list
 
 Each case is launched `reps` times from one captured CUDA graph (no host
@@ -13,6 +14,7 @@ summaries in profiles/.
 """
 
 import argparse
+import ctypes
 import json
 
 import numpy as np
@@ -121,6 +123,40 @@ def decode_products(batch=32, layers=30, hidden=576, inter=1536, q_out=576, kv_o
     return launch, total, 4 * layers + 1
 
 
+def mlp_case(reps):
+    """C2: the 4-block int8 MLP chain at batch 256 (17.2 GFLOP of products):
+    per block Gelu(x @ W1), (h @ W2) + x, RmsNorm; one CUDA graph."""
+    x, blocks = syn.mlp_stack()
+    dev = [tuple(torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in b) for b in blocks]
+    h0 = torch.from_numpy(x).cuda()
+    m, hidden = h0.shape
+    inter = blocks[0][0].shape[1]
+    t = torch.empty(m, inter, device="cuda")
+    s = torch.empty(m, hidden, device="cuda")
+    hs = [torch.empty(m, hidden, device="cuda") for _ in dev]
+    lib = K.load()
+    work = torch.zeros(max(lib.accel_b200_matmul_q8_workspace(m, hidden, inter),
+                           lib.accel_b200_matmul_q8_workspace(m, inter, hidden)), dtype=torch.uint8, device="cuda")
+    gelu = K.make_epilogue(act="gelu")
+    res = [K.make_epilogue(residual=h0 if i == 0 else hs[i - 1]) for i in range(len(dev))]
+
+    def launch(_):
+        h = h0
+        for i, (w1, s1, w2, s2, gamma) in enumerate(dev):
+            K.matmul_q8(h, w1, s1, epilogue=gelu, out=t, workspace=work)
+            K.matmul_q8(t, w2, s2, epilogue=res[i], out=s, workspace=work)
+            check_rc = lib.accel_b200_rmsnorm(K._p(s), K._p(gamma), K._p(hs[i]), m, hidden, ctypes.c_float(1e-5), 0,
+                                              K._s())
+            assert check_rc == 0
+            h = hs[i]
+
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        us = _time_graph(launch, reps, stream)
+    flops = 4 * 2 * (2.0 * m * hidden * inter)
+    return {"case": "c2_mlp_4blocks_b256", "us": round(us, 2), "tflops": round(flops / us / 1e6, 1)}
+
+
 def step_case(reps):
     stream = torch.cuda.Stream()
     launch, nbytes, count = decode_products()
@@ -176,7 +212,7 @@ def attention_case(batch, length, reps, kind="fused", context=2048, heads=9, kv_
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "step", "list"])
+    ap.add_argument("what", choices=["gemm", "attention", "step", "mlp", "list"])
     ap.add_argument("--path", default="auto", choices=["auto", "tc", "gemv", "simt"])
     ap.add_argument("--shapes", default="decode", choices=["decode", "prefill", "c5", "all"])
     ap.add_argument("--batch", type=int, default=32)
@@ -199,6 +235,8 @@ def main():
                 reps = args.reps if m * k * n < 1e10 else max(3, args.reps // 10)
                 print(json.dumps(dict(gemm_case(name, m, k, n, reps), path=args.path)), flush=True)
         K.set_q8_path(0)
+    elif args.what == "mlp":
+        print(json.dumps(mlp_case(args.reps)), flush=True)
     elif args.what == "step":
         print(json.dumps(step_case(args.reps)), flush=True)
     else:

@@ -120,3 +120,28 @@ def test_empty_k(lib, cuda):
     got = H(K.matmul_q8(T(np.zeros((3, 0), np.float32)), T(np.zeros((0, 4), np.int8)), T(np.ones(4, np.float32)),
                         epilogue=K.make_epilogue(alpha=2.0)))
     assert got.tolist() == [[0.0] * 4] * 3
+
+
+def c2_chain_gpu(x, blocks, rows):
+    """C2 on the device: per block h = Gelu(x @ W1) (fused Gelu epilogue),
+    s = h @ W2 + x (fused residual), x' = RmsNorm(s) (eps 1e-5)."""
+    h = T(x[:rows])
+    for w1, s1, w2, s2, gamma in blocks:
+        t = K.matmul_q8(h, T(w1), T(s1), epilogue=K.make_epilogue(act="gelu"))
+        s = K.matmul_q8(t, T(w2), T(s2), epilogue=K.make_epilogue(residual=h))
+        h = K.rmsnorm(s, T(gamma), rows, s.shape[1], 1e-5)
+    return H(h)
+
+
+def test_c2_mlp_chain(lib, cuda, orc):
+    """Config C2, the whole 4-block chain at batch 256 (hidden 1024 -> 4096 ->
+    1024; the rows run on the tensor cores), against the CPU checker's
+    block-by-block chain (src/ep.cc:1602-1626 order) on all 256 rows and
+    against the stored 16-row golden of the reference chain."""
+    x, blocks = syn.mlp_stack()
+    got = c2_chain_gpu(x, blocks, 256)
+    want = x.copy()
+    for w1, s1, w2, s2, gamma in blocks:
+        want, _ = orc.mlp_block(want, w1, s1, w2, s2, gamma, 1e-5)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(got[:16], np.load(GOLDEN / "ref_small.npz")["c2_rows16"], rtol=1e-4, atol=1e-4)
