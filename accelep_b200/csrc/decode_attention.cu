@@ -41,6 +41,7 @@ namespace {
 constexpr int kD = 64;          // head_dim
 constexpr int kRows = 64;       // context rows per chunk
 constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
 constexpr int kMaxG = 8;        // query heads per kv head
 constexpr int kMaxSplit = 8;    // CTAs per cluster
 constexpr int kChunkFloats = kRows * kD;
@@ -69,11 +70,12 @@ struct FusedArgs {
 template <int G>
 __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a) {
   extern __shared__ __align__(128) float buf[];  // [2][K | V][64 rows][64]
-  __shared__ __align__(8) uint64_t full[2];
-  __shared__ __align__(16) float qs[G * kD];  // roped query heads
-  __shared__ __align__(16) float ps[G * kRows];  // scores, then weights, of the current chunk
-  __shared__ __align__(16) float mo[G * kD];  // published weighted values
-  __shared__ float m_run[G], l_run[G], corr[G];
+  __shared__ __align__(8) uint64_t full[2], empty[2];
+  __shared__ __align__(16) float qs[G * kD];        // roped query heads
+  __shared__ __align__(16) float wo[kWarps][G * kD];  // per-warp weighted values
+  __shared__ float wm[kWarps][G], wl[kWarps][G];    // per-warp running max and sum
+  __shared__ __align__(16) float mo[G * kD];        // published weighted values
+  __shared__ float m_run[G], l_run[G];
   __shared__ int32_t ok_s;
   PdlTrigger();
   PdlWait();  // row positions, q|k|v rows and the cache come from earlier kernels
@@ -96,13 +98,11 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   const float* row = a.qkv + r * a.qkv_ld;
 
   if (tid == 0) {
-    MbarInit(&full[0], 1);
-    MbarInit(&full[1], 1);
+    for (int b = 0; b < 2; ++b) {
+      MbarInit(&full[b], 1);
+      MbarInit(&empty[b], kWarps);
+    }
     FenceBarrierInit();
-  }
-  if (tid < G) {
-    m_run[tid] = -INFINITY;
-    l_run[tid] = 0.f;
   }
   __syncthreads();
 
@@ -143,12 +143,22 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   }
   __syncthreads();
 
-  // Weighted values: thread (d = tid % 64, half = tid / 64) owns heads
-  // half, half + 2, ... of dimension d.
-  const int d = tid & (kD - 1), vh = tid >> 6;
-  float acc[(G + 1) / 2];
+  // Warp w owns rows 16w .. 16w + 15 of every chunk and keeps its own online
+  // softmax: lane pair (2j, 2j + 1) scores row 16w + j (each lane over half of
+  // the dimensions), and every lane accumulates dimensions lane and lane + 32
+  // of the weighted values for all G heads. No CTA barrier per chunk: a warp
+  // frees a buffer through `empty`, and the producer (thread 0) refills it once
+  // all four warps are done with it.
+  constexpr int kWarpRows = kRows / kWarps;
+  const int wr0 = warp * kWarpRows;
+  float m_w[G], l_w[G], o[G][2];
 #pragma unroll
-  for (int j = 0; j < (G + 1) / 2; ++j) acc[j] = 0.f;
+  for (int hh = 0; hh < G; ++hh) {
+    m_w[hh] = -INFINITY;
+    l_w[hh] = 0.f;
+    o[hh][0] = 0.f;
+    o[hh][1] = 0.f;
+  }
   bool ok = true;
 
   for (int i = 0; i < nloc; ++i) {
@@ -157,35 +167,34 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
     const int64_t t0 = static_cast<int64_t>(c_begin + i) * kRows;
     const int cnt = static_cast<int>(Min64(kRows, len - t0));
     ok &= MbarWait(&full[i & 1], (i >> 1) & 1);
-    if (t0 + cnt == len) {
-      // The new row: RoPE on its key, append key and value to the cache, and
-      // place both in the buffer as row cnt - 1.
+    if (t0 + cnt == len && (cnt - 1) / kWarpRows == warp) {
+      // The new row lies in this warp's rows: RoPE on its key, append key and
+      // value to the cache, and place both in the buffer as row cnt - 1.
       const float* c = a.cos_t + pos * kD;
       const float* s = a.sin_t + pos * kD;
       const float* kin = row + static_cast<int64_t>(a.heads + g) * kD;
       const float* vin = row + static_cast<int64_t>(a.heads + a.kv_heads + g) * kD;
-      if (tid < kD / 2) {
-        float lo, hi;
-        RopePair(kin[tid], kin[kD / 2 + tid], c, s, tid, kD / 2, &lo, &hi);
-        kb[(cnt - 1) * kD + tid] = lo;
-        kb[(cnt - 1) * kD + kD / 2 + tid] = hi;
-        kbase[pos * kD + tid] = lo;
-        kbase[pos * kD + kD / 2 + tid] = hi;
-      } else if (tid >= 64) {
-        const float v = vin[tid - 64];
-        vb[(cnt - 1) * kD + tid - 64] = v;
-        vbase[pos * kD + tid - 64] = v;
-      }
-      __syncthreads();
+      float lo, hi;
+      RopePair(kin[lane], kin[kD / 2 + lane], c, s, lane, kD / 2, &lo, &hi);
+      kb[(cnt - 1) * kD + lane] = lo;
+      kb[(cnt - 1) * kD + kD / 2 + lane] = hi;
+      kbase[pos * kD + lane] = lo;
+      kbase[pos * kD + kD / 2 + lane] = hi;
+      const float v0 = vin[lane], v1 = vin[lane + 32];
+      vb[(cnt - 1) * kD + lane] = v0;
+      vb[(cnt - 1) * kD + lane + 32] = v1;
+      vbase[pos * kD + lane] = v0;
+      vbase[pos * kD + lane + 32] = v1;
+      __syncwarp();
     }
-    // Scores: two threads per row, each over half of the dimensions; the
-    // float4 index rotates with the row so a quarter-warp hits 32 banks.
-    {
-      const int j = tid >> 1, half = tid & 1;
+    if (wr0 < cnt) {
+      // Scores of row j: the float4 index rotates with the row so a
+      // quarter-warp hits 32 banks.
+      const int j = wr0 + (lane >> 1), half = lane & 1;
       const bool valid = j < cnt;
-      float dot[G];
+      float sc[G];
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh) dot[hh] = 0.f;
+      for (int hh = 0; hh < G; ++hh) sc[hh] = 0.f;
       if (valid) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -194,52 +203,46 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
 #pragma unroll
           for (int hh = 0; hh < G; ++hh) {
             const float4 qv = *reinterpret_cast<const float4*>(qs + hh * kD + d4 * 4);
-            dot[hh] = fmaf(qv.x, kv.x, dot[hh]);
-            dot[hh] = fmaf(qv.y, kv.y, dot[hh]);
-            dot[hh] = fmaf(qv.z, kv.z, dot[hh]);
-            dot[hh] = fmaf(qv.w, kv.w, dot[hh]);
+            sc[hh] = fmaf(qv.x, kv.x, sc[hh]);
+            sc[hh] = fmaf(qv.y, kv.y, sc[hh]);
+            sc[hh] = fmaf(qv.z, kv.z, sc[hh]);
+            sc[hh] = fmaf(qv.w, kv.w, sc[hh]);
           }
         }
       }
+      float p[G];
 #pragma unroll
       for (int hh = 0; hh < G; ++hh) {
-        const float other = __shfl_xor_sync(kFull, dot[hh], 1);
-        if (valid && half == 0) ps[hh * kRows + j] = (dot[hh] + other) * a.scale;
+        const float full_dot = sc[hh] + __shfl_xor_sync(kFull, sc[hh], 1);
+        const float x = valid ? full_dot * a.scale : -INFINITY;
+        const float mx = fmaxf(WarpMax(x), m_w[hh]);  // finite: row wr0 < cnt is valid
+        p[hh] = valid ? expf(x - mx) : 0.f;
+        const float sum = WarpSum(half == 0 ? p[hh] : 0.f);
+        const float corr = expf(m_w[hh] - mx);  // 0 on this warp's first rows
+        l_w[hh] = l_w[hh] * corr + sum;
+        m_w[hh] = mx;
+        o[hh][0] *= corr;
+        o[hh][1] *= corr;
       }
-    }
-    __syncthreads();
-    // Online softmax per head: new max, weights of this chunk, rescale factor.
-    for (int hh = warp; hh < G; hh += kThreads / 32) {
-      float mx = -INFINITY;
-      for (int j = lane; j < cnt; j += 32) mx = fmaxf(mx, ps[hh * kRows + j]);
-      mx = fmaxf(WarpMax(mx), m_run[hh]);
-      float sum = 0.f;
-      for (int j = lane; j < cnt; j += 32) {
-        const float p = expf(ps[hh * kRows + j] - mx);
-        ps[hh * kRows + j] = p;
-        sum += p;
-      }
-      sum = WarpSum(sum);
-      if (lane == 0) {
-        const float f = expf(m_run[hh] - mx);  // 0 on the first chunk
-        corr[hh] = f;
-        l_run[hh] = l_run[hh] * f + sum;
-        m_run[hh] = mx;
-      }
-    }
-    __syncthreads();
+      const int rows = min(kWarpRows, cnt - wr0);
+#pragma unroll 4
+      for (int rr = 0; rr < rows; ++rr) {
+        const float v0 = vb[(wr0 + rr) * kD + lane];
+        const float v1 = vb[(wr0 + rr) * kD + lane + 32];
 #pragma unroll
-    for (int j = 0; j < (G + 1) / 2; ++j) {
-      const int hh = vh + 2 * j;
-      if (hh < G) {
-        const float* p = ps + hh * kRows;
-        float o = 0.f;
-        for (int t = 0; t < cnt; ++t) o = fmaf(p[t], vb[t * kD + d], o);
-        acc[j] = acc[j] * corr[hh] + o;
+        for (int hh = 0; hh < G; ++hh) {
+          const float pr = __shfl_sync(kFull, p[hh], 2 * rr);
+          o[hh][0] = fmaf(pr, v0, o[hh][0]);
+          o[hh][1] = fmaf(pr, v1, o[hh][1]);
+        }
       }
     }
-    __syncthreads();  // buffer i & 1 and the weights are free
-    if (tid == 0 && i + 2 < nloc) issue(i + 2);
+    __syncwarp();
+    if (lane == 0) MbarArrive(&empty[i & 1]);
+    if (tid == 0 && i + 2 < nloc) {
+      ok &= MbarWait(&empty[i & 1], (i >> 1) & 1);  // all warps are done with this buffer
+      issue(i + 2);
+    }
   }
   ok = __syncthreads_and(ok);
   if (!ok) {
@@ -247,10 +250,36 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
     // Copies still in flight land before the CTA leaves (bounded waits).
     for (int i = 0; i < nloc && i < 2; ++i) MbarWait(&full[i & 1], ((nloc - 1 - i) >> 1) & 1);
   }
+  // The four warp states -> one CTA state (log-sum-exp, warps in order).
 #pragma unroll
-  for (int j = 0; j < (G + 1) / 2; ++j) {
-    const int hh = vh + 2 * j;
-    if (hh < G) mo[hh * kD + d] = acc[j];
+  for (int hh = 0; hh < G; ++hh) {
+    wo[warp][hh * kD + lane] = o[hh][0];
+    wo[warp][hh * kD + lane + 32] = o[hh][1];
+    if (lane == 0) {
+      wm[warp][hh] = m_w[hh];
+      wl[warp][hh] = l_w[hh];
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < G * kD; e += kThreads) {
+    const int hh = e / kD;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, wm[w][hh]);
+    float l = 0.f, acc = 0.f;
+    if (mx != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float f = expf(wm[w][hh] - mx);
+        l = fmaf(wl[w][hh], f, l);
+        acc = fmaf(wo[w][e], f, acc);
+      }
+    }
+    mo[e] = acc;
+    if ((e & (kD - 1)) == 0) {
+      m_run[hh] = mx;
+      l_run[hh] = l;
+    }
   }
   if (tid == 0) ok_s = ok ? 1 : 0;
   ClusterSync();  // every rank's state is published

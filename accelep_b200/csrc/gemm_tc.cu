@@ -716,7 +716,13 @@ template <int R, int M>
 int LaunchTcStages(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
                    const TcPlan& p, cudaStream_t s) {
   if (p.stages == 2) return LaunchTc<R, 2, M>(tw, tx, tu, g, p, s);
-  return LaunchTc<R, MaxStages<R, M>(), M>(tw, tx, tu, g, p, s);
+  // Long weight streams with few rows (planes mode, R = 32): three stages
+  // leave room for two CTAs per SM, doubling the converter warps per SM.
+  if constexpr (R == 32 && M == kAPlanes) {
+    return LaunchTc<R, 3, M>(tw, tx, tu, g, p, s);
+  } else {
+    return LaunchTc<R, MaxStages<R, M>(), M>(tw, tx, tu, g, p, s);
+  }
 }
 
 bool Encode2D(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t outer,
