@@ -76,7 +76,6 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   __shared__ float wm[kWarps][G], wl[kWarps][G];    // per-warp running max and sum
   __shared__ __align__(16) float mo[G * kD];        // published weighted values
   __shared__ float m_run[G], l_run[G];
-  __shared__ int32_t ok_s;
   PdlTrigger();
   PdlWait();  // row positions, q|k|v rows and the cache come from earlier kernels
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -278,24 +277,38 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
     mo[e] = acc;
     if ((e & (kD - 1)) == 0) {
       m_run[hh] = mx;
-      l_run[hh] = l;
+      l_run[hh] = ok ? l : __int_as_float(0x7fc00000);
     }
   }
-  if (tid == 0) ok_s = ok ? 1 : 0;
   ClusterSync();  // every rank's state is published
-  bool all_ok = true;
-  for (int p = 0; p < S; ++p) all_ok &= LoadPeerInt(&ok_s, static_cast<uint32_t>(p)) != 0;
-  if (all_ok && pos >= 0) {
-    // Rank `rank` merges outputs rank, rank + S, ... of the G * 64.
+  if (pos >= 0) {
+    // Rank `rank` merges outputs rank, rank + S, ... of the G * 64: every
+    // peer's state is loaded first (one round trip), then combined in rank
+    // order. A rank whose wait ran out published a NaN sum, so its tile's
+    // outputs are NaN (and the status word carries the timeout bit).
     for (int e = rank * kThreads + tid; e < G * kD; e += S * kThreads) {
       const int hh = e / kD;
+      float pm[kMaxSplit], pl[kMaxSplit], po[kMaxSplit];
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p) {
+        if (p < S) {
+          pm[p] = LoadPeer(&m_run[hh], static_cast<uint32_t>(p));
+          pl[p] = LoadPeer(&l_run[hh], static_cast<uint32_t>(p));
+          po[p] = LoadPeer(&mo[e], static_cast<uint32_t>(p));
+        }
+      }
       float mx = -INFINITY;
-      for (int p = 0; p < S; ++p) mx = fmaxf(mx, LoadPeer(&m_run[hh], static_cast<uint32_t>(p)));
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < S) mx = fmaxf(mx, pm[p]);
       float l = 0.f, o = 0.f;
-      for (int p = 0; p < S; ++p) {
-        const float w = expf(LoadPeer(&m_run[hh], static_cast<uint32_t>(p)) - mx);
-        l = fmaf(LoadPeer(&l_run[hh], static_cast<uint32_t>(p)), w, l);
-        o = fmaf(LoadPeer(&mo[e], static_cast<uint32_t>(p)), w, o);
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p) {
+        if (p < S) {
+          const float w = expf(pm[p] - mx);
+          l = fmaf(pl[p], w, l);
+          o = fmaf(po[p], w, o);
+        }
       }
       a.out[r * a.out_ld + static_cast<int64_t>(h0) * kD + e] = o / l;
     }

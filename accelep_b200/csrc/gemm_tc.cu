@@ -301,7 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t full_w[kMaxStages], full_x[kMaxStages], empty[kMaxStages], cfull[kConvBufs],
       cempty[kConvBufs], accf;
   __shared__ uint32_t tmem_s;
-  __shared__ int32_t ok_s;
   __shared__ double inv_s[M == kANorm ? R : 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t raw_addr = SmemAddr(smem_raw);
@@ -443,11 +442,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!cta_ok) {
     // A wait ran out: report it and let the tensor core finish (bounded). The
     // CTA still takes part in the cluster barriers below, so that no peer
-    // waits for it, but the tile is not written.
+    // waits for it. Unsplit, its tile is not written; split, its partial tile
+    // is NaN, so the tile it feeds is NaN.
     if (tid == 0 && g.status != nullptr) atomicOr(g.status, ACCEL_B200_STATUS_COPY_TIMEOUT);
     if (nkb > 0) MbarWait(&accf, 0);
   }
-  if (tid == 0) ok_s = cta_ok ? 1 : 0;
   TcFenceAfterSync();
   // Split K runs as one thread-block cluster along grid y; every CTA of the
   // cluster holds its partial tile in shared memory and the cluster sums the
@@ -456,13 +455,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t rows = Min64(R, g.m - row0);
   const int64_t cols = Min64(kBn, g.n - n0);
   float* tile = reinterpret_cast<float*>(smem);  // [R][128] fp32; the stage memory is idle now
-  if (warp >= 2 && cta_ok) {
+  if (warp >= 2) {
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. +31
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
     for (int c0 = 0; c0 < R; c0 += 32) {
       float v[32];
-      if (nkb > 0) {
+      if (nkb > 0 && cta_ok) {
         // hi + mid + lo, each accumulated separately over K.
         float w[32];
         TmemLoad32(lane_base + c0, v);
@@ -474,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 32; ++j) v[j] += w[j];
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        for (int j = 0; j < 32; ++j) v[j] = cta_ok ? 0.f : __int_as_float(0x7fc00000);
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) tile[(c0 + j) * kBn + quarter * 32 + lane] = v[j];
@@ -512,11 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int j = 0; j < 4; ++j) {
     sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
   }
-  ClusterSync();  // every partial tile (and ok flag) of the cluster is complete
-  bool all_ok = true;
-  for (int p = 0; p < splits; ++p) all_ok &= LoadPeerInt(&ok_s, static_cast<uint32_t>(p)) != 0;
+  ClusterSync();  // every partial tile of the cluster is complete
   float4 sum[kMaxJ];
-  if (all_ok && c4 < cols) {
+  if (c4 < cols) {
 #pragma unroll
     for (int j = 0; j < kMaxJ; ++j) {
       const int r = r_begin + j * (kThreads / 32);
@@ -545,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // This CTA has read what it needs from its peers: arrive now, and wait for
   // the peers' reads of this CTA's tile only before leaving.
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  if (all_ok && c4 < cols) {
+  if (c4 < cols) {
 #pragma unroll
     for (int j = 0; j < kMaxJ; ++j) {
       const int r = r_begin + j * (kThreads / 32);
