@@ -24,13 +24,19 @@
 #include "accel_b200_contract.h"
 #endif
 
+#if defined(__GNUC__)
+#define ACCEL_B200_CXX_API __attribute__((visibility("default")))
+#else
+#define ACCEL_B200_CXX_API
+#endif
+
 namespace accel_b200 {
 
 // Creates a device on CUDA ordinal `ordinal` (-1: the current device).
 // Throws std::runtime_error when no CUDA device is usable.
-std::unique_ptr<accel::Device> CreateB200Device(int ordinal = -1);
+ACCEL_B200_CXX_API std::unique_ptr<accel::Device> CreateB200Device(int ordinal = -1);
 
 // Process-wide count of B200Device allocations not yet freed.
-int64_t LiveB200Allocs();
+ACCEL_B200_CXX_API int64_t LiveB200Allocs();
 
 }  // namespace accel_b200
