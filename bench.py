@@ -44,10 +44,11 @@ PROMPT_SEED = 41
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
 # DRAM bytes (read + write) per launch from ncu captures of the same launches
-# (profiles/q8_product_decode_step.md, profiles/decode_attention_b32_len1280.md);
-# None until captured.
-PRODUCT_TRAFFIC = None
-ATTENTION_TRAFFIC = 63_521_280
+# (profiles/q8_product_decode_qkv_m32.md: one decode step's products, 168.9 MB
+# over 121 products; profiles/decode_attention_b32_len1280.md).
+PRODUCT_TRAFFIC = 1_395_815
+ATTENTION_TRAFFIC = 63_610_368
+GEMV_TRAFFIC = 274_861_568  # profiles/q8_gemv_c5_m1_k16384.md
 
 
 def config(n):
@@ -438,7 +439,7 @@ def run_b200(args):
                                            "copies rotated (512 MB > L2)",
                                  "us_per_launch": gemv["us"], "achieved": gemv["gbs"], "peak": peak,
                                  "peak_kind": peak_kind, "unit": "GB/s", "frac": gemv["gbs"] / peak,
-                                 "bytes_per_launch": 16384 * 16384 + 4 * 16384 * 3},
+                                 "bytes_per_launch": 16384 * 16384 + 4 * 16384 * 3, "traffic": GEMV_TRAFFIC},
                 "c5_sharded": {"what": "int8 GEMM sweep points with W N-sharded over the ranks; one call = local "
                                        "product + assembly of Y on every rank (nccl: all_gather_into_tensor + "
                                        "transpose; fused: peer stores from the product epilogue + peer-memory "
