@@ -29,7 +29,8 @@ class Epilogue(ctypes.Structure):
     """accel_b200_epilogue (include/accel_b200.h)."""
 
     _fields_ = [("alpha", c_f32), ("beta", c_f32), ("bias", c_vp), ("bias_row_stride", c_i64),
-                ("bias_col_stride", c_i64), ("act", c_i32), ("residual", c_vp), ("residual_ld", c_i64)]
+                ("bias_col_stride", c_i64), ("act", c_i32), ("residual", c_vp), ("residual_ld", c_i64),
+                ("row_sq", c_vp), ("row_sq_ld", c_i64)]
 
 
 class LlamaConfig(ctypes.Structure):
@@ -70,6 +71,8 @@ SIGNATURES = {
     "accel_b200_matmul_q8_rmsnorm_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_q8_rmsnorm": (c_int, [c_vp, c_i64, c_vp, c_f32, P_plane, c_vp, c_i64, c_i64, c_i64, c_i64,
                                              P_ep, c_vp, c_sz, c_vp]),
+    "accel_b200_matmul_q8_rmsnorm_stats": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_f32, P_plane, c_vp,
+                                                   c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_matmul_f32_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_f32": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_rope_append": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,

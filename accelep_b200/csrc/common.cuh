@@ -128,6 +128,8 @@ struct Epilogue {
   int32_t act = 0;
   const float* residual = nullptr;
   int64_t residual_ld = 0;
+  double* row_sq = nullptr;  // per row and 128-column block: sum of squares of the outputs
+  int64_t row_sq_ld = 0;
 };
 
 __device__ __forceinline__ float ApplyEpilogue(const Epilogue& ep, float acc, int64_t i, int64_t j) {

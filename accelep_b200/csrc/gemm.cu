@@ -316,6 +316,8 @@ bool ToEpilogue(const accel_b200_epilogue* in, Epilogue* out) {
   out->act = in->act;
   out->residual = in->residual;
   out->residual_ld = in->residual_ld;
+  out->row_sq = in->row_sq;
+  out->row_sq_ld = in->row_sq_ld;
   return in->act >= 0 && in->act <= 2;
 }
 
@@ -344,7 +346,7 @@ size_t TcWorkspace(int64_t m, int64_t k, int64_t n);
 int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
           const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
           const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream,
-          const PeerOut* peers);
+          const PeerOut* peers, const double* sq_in, int64_t sq_ld, int32_t sq_n);
 int LaunchRmsNormRows(const float* x, int64_t ldx, const float* w, float* y, int64_t ldy, int64_t rows, int64_t dim,
                       float eps, int64_t row_offset, cudaStream_t stream);
 int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
@@ -400,12 +402,13 @@ int MatMulQ8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c
   }
   if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
     return RunTc(a, nullptr, lda, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace,
-                 workspace_bytes, nullptr, AsStream(stream), peers);
+                 workspace_bytes, nullptr, AsStream(stream), peers, nullptr, 0, 0);
   }
-  if (with_peers) {
+  if (with_peers || g.ep.row_sq != nullptr) {
     return SetError(ACCEL_B200_EINVAL,
-                    "matmul_q8_peers: needs the GEMV or tensor-core path (per-column or single scale, no zero "
-                    "points, 16-byte aligned rows, k % 8 == 0 and n % 16 == 0 above m = 8)");
+                    "matmul_q8: peer outputs and row sums of squares need the GEMV or tensor-core path "
+                    "(per-column or single scale, no zero points, 16-byte aligned rows, k % 8 == 0 and n % 16 == 0 "
+                    "above m = 8)");
   }
   g.a = a;
   g.lda = lda;
@@ -510,7 +513,7 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
   if (inter % 4 == 0 && UseTc(gate_up, ld, w, b->axis, b->zero, m, inter, n) &&
       reinterpret_cast<uintptr_t>(up) % 16 == 0) {
     return RunTc(gate_up, up, ld, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, inter, n, e, workspace,
-                 workspace_bytes, nullptr, AsStream(stream), nullptr);
+                 workspace_bytes, nullptr, AsStream(stream), nullptr, nullptr, 0, 0);
   }
   // CUDA cores: SiluMul rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * inter * sizeof(float);
@@ -527,10 +530,10 @@ ACCEL_B200_API size_t accel_b200_matmul_q8_rmsnorm_workspace(int64_t m, int64_t 
   return base + static_cast<size_t>(m > 0 ? m : 0) * static_cast<size_t>(k > 0 ? k : 0) * sizeof(float);
 }
 
-ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, const float* gamma, float eps,
-                                                const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
-                                                int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,
-                                                size_t workspace_bytes, void* stream) {
+static int MatMulQ8RmsNorm(const float* x, int64_t ldx, const double* sq, int64_t sq_ld, int32_t sq_n,
+                           const float* gamma, float eps, const accel_b200_q8_plane* b, float* c, int64_t ldc,
+                           int64_t m, int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   if (m < 0 || k < 0 || n < 0 || b == nullptr || ldx < k) {
     return SetError(ACCEL_B200_EINVAL, "quantized MatMul (RmsNorm rows) is out of range");
   }
@@ -550,7 +553,7 @@ ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, con
   const int8_t* w = b->q + b->offset;
   if (UseTc(x, ldx, w, b->axis, b->zero, m, k, n) && reinterpret_cast<uintptr_t>(gamma) % 16 == 0) {
     return RunTc(x, nullptr, ldx, gamma, eps, w, b->scale, b->axis < 0, c, ldc, m, k, n, e, workspace,
-                 workspace_bytes, nullptr, AsStream(stream), nullptr);
+                 workspace_bytes, nullptr, AsStream(stream), nullptr, sq, sq_ld, sq_n);
   }
   // CUDA cores: RmsNorm rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * k * sizeof(float);
@@ -558,6 +561,26 @@ ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, con
   const int rc = LaunchRmsNormRows(x, ldx, gamma, act, k, m, k, eps, 0, AsStream(stream));
   if (rc != ACCEL_B200_OK) return rc;
   return accel_b200_matmul_q8(act, k, b, c, ldc, m, k, n, ep, workspace, base, stream);
+}
+
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, const float* gamma, float eps,
+                                                const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
+                                                int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+  return MatMulQ8RmsNorm(x, ldx, nullptr, 0, 0, gamma, eps, b, c, ldc, m, k, n, ep, workspace, workspace_bytes,
+                         stream);
+}
+
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm_stats(const float* x, int64_t ldx, const double* row_sq,
+                                                      int64_t row_sq_ld, int32_t row_sq_n, const float* gamma,
+                                                      float eps, const accel_b200_q8_plane* b, float* c, int64_t ldc,
+                                                      int64_t m, int64_t k, int64_t n, const accel_b200_epilogue* ep,
+                                                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (row_sq == nullptr || row_sq_n <= 0 || row_sq_ld < row_sq_n) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_rmsnorm_stats: bad row sums of squares");
+  }
+  return MatMulQ8RmsNorm(x, ldx, row_sq, row_sq_ld, row_sq_n, gamma, eps, b, c, ldc, m, k, n, ep, workspace,
+                         workspace_bytes, stream);
 }
 
 ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const float* b, float* c, int64_t ldc, int64_t m,
@@ -570,6 +593,7 @@ ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const floa
   if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "MatMul: bad output");
   if (k == 0) return EmptySum(c, ldc, m, n, g.ep, AsStream(stream));
   if (a == nullptr || b == nullptr || lda < k) return SetError(ACCEL_B200_EINVAL, "MatMul is missing an operand");
+  if (g.ep.row_sq != nullptr) return SetError(ACCEL_B200_EINVAL, "MatMul: row sums of squares need int8 weights");
   g.a = a;
   g.lda = lda;
   g.w = b;

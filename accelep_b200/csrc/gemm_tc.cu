@@ -95,6 +95,9 @@ struct TcArgs {
   int64_t lda;
   const float* gamma;  // norm mode: RmsNorm weights [k]
   float eps;
+  const double* sq_in;  // norm mode, optional: per row, sq_n partial sums of squares (stride sq_ld)
+  int64_t sq_ld;
+  int32_t sq_n;
   int64_t m, k, n;
   int32_t kb_total;
   int32_t kb_per_split;
@@ -410,9 +413,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if constexpr (M == kANorm) {
-      // Row RMS of the valid rows (whole rows of A).
+      // Row RMS of the valid rows: from the producer's sums of squares when
+      // given, else from the whole rows of A.
       PdlWait();
-      TileInverseRms<R>(g.a, g.lda, row0, valid, g.k, g.eps, ct, inv_s);
+      if (g.sq_in != nullptr) {
+        if (ct < valid) {
+          const double* p = g.sq_in + (row0 + ct) * g.sq_ld;
+          double sum = 0.0;
+          for (int t = 0; t < g.sq_n; ++t) sum += p[t];
+          inv_s[ct] = 1.0 / sqrt(sum / static_cast<double>(g.k) + static_cast<double>(g.eps));
+        }
+      } else {
+        TileInverseRms<R>(g.a, g.lda, row0, valid, g.k, g.eps, ct, inv_s);
+      }
       asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
     }
     for (int i = 0; i < nkb; ++i) {
@@ -493,9 +506,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float o = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
         g.c[row * g.ldc + col] = o;
         StorePeers(g.peers, row * g.ldc + col, o);
+        if (g.ep.row_sq != nullptr) tile[r * kBn + tid] = o;
       }
     }
     if (g.peers.n > 0) __threadfence_system();
+    if (g.ep.row_sq != nullptr) {
+      // Sums of squares of this tile's outputs per row: warp w of the first
+      // four takes rows w, w + 4, ...; lane l the columns 4l .. 4l + 3.
+      __syncthreads();
+      if (tid < 128 && cta_ok) {
+        for (int r = warp; r < rows; r += 4) {
+          double sq = 0.0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (lane * 4 + q < cols) {
+              const double v = static_cast<double>(tile[r * kBn + lane * 4 + q]);
+              sq += v * v;
+            }
+          }
+          sq = WarpSum(sq);
+          if (lane == 0) g.ep.row_sq[(row0 + r) * g.ep.row_sq_ld + n0 / kBn] = sq;
+        }
+      }
+    }
     return;
   }
   // Rank `rank` sums rows [rank * rpr, +rpr) of the tile over the cluster; a
@@ -542,16 +575,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   // This CTA has read what it needs from its peers: arrive now, and wait for
   // the peers' reads of this CTA's tile only before leaving.
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  if (c4 < cols) {
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
-      const int r = r_begin + j * (kThreads / 32);
-      if (r < r_end) {
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int r = r_begin + j * (kThreads / 32);  // the same for the 32 lanes of a warp
+    if (r < r_end) {
+      double sq = 0.0;
+      if (c4 < cols) {
         const int64_t row = row0 + r;
         const float v[4] = {sum[j].x, sum[j].y, sum[j].z, sum[j].w};
         float o[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (c4 + q < cols) {
+            const double dv = static_cast<double>(o[q]);
+            sq += dv * dv;
+          }
+        }
         const int64_t off = row * g.ldc + n0 + c4;
         float* dst = g.c + off;
         if (g.vec_store && c4 + 4 <= cols) {
@@ -566,6 +607,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      }
+      if (g.ep.row_sq != nullptr) {  // the warp holds the row's 128 columns of this tile
+        sq = WarpSum(sq);
+        if (lane == 0) g.ep.row_sq[(row0 + r) * g.ep.row_sq_ld + n0 / kBn] = sq;
       }
     }
   }
@@ -758,7 +803,7 @@ size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
 int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
           const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
           const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream,
-          const PeerOut* peers) {
+          const PeerOut* peers, const double* sq_in, int64_t sq_ld, int32_t sq_n) {
   const TcPlan p = MakeTcPlan(m, k, n, up != nullptr, gamma != nullptr);
   if (p.planes_bytes > 0 && (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes)) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
@@ -805,6 +850,9 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   g.lda = lda;
   g.gamma = gamma;
   g.eps = eps;
+  g.sq_in = sq_in;
+  g.sq_ld = sq_ld;
+  g.sq_n = sq_n;
   g.m = m;
   g.k = k;
   g.n = n;

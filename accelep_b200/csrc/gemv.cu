@@ -203,28 +203,43 @@ __global__ void __launch_bounds__(kGvThreads) Q8GemvKernel(GemvArgs g) {
     } else {
       s = *reinterpret_cast<const float4*>(cta_sum + r * SW + cl);
     }
-    if (r >= rows || col >= g.n) continue;
-    const int64_t row = row0 + r;
-    const float v[4] = {s.x, s.y, s.z, s.w};
-    float o[4];
+    double sq = 0.0;
+    if (r < rows && col < g.n) {
+      const int64_t row = row0 + r;
+      const float v[4] = {s.x, s.y, s.z, s.w};
+      float o[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float scq = g.scalar_scale ? __ldg(g.scale) : (col + q < g.n ? __ldg(g.scale + col + q) : 0.f);
-      o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], scq), row, col + q);
-    }
-    const int64_t off = row * g.ldc + col;
-    float* dst = g.c + off;
-    if (g.vec_store && col + 4 <= g.n) {
-      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-      StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
-    } else {
+      for (int q = 0; q < 4; ++q) {
+        const float scq = g.scalar_scale ? __ldg(g.scale) : (col + q < g.n ? __ldg(g.scale + col + q) : 0.f);
+        o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], scq), row, col + q);
+      }
+      const int64_t off = row * g.ldc + col;
+      float* dst = g.c + off;
+      if (g.vec_store && col + 4 <= g.n) {
+        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (col + q < g.n) {
+            dst[q] = o[q];
+            StorePeers(g.peers, off + q, o[q]);
+          }
+        }
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (col + q < g.n) {
-          dst[q] = o[q];
-          StorePeers(g.peers, off + q, o[q]);
+          const double dv = static_cast<double>(o[q]);
+          sq += dv * dv;
         }
       }
+    }
+    if (g.ep.row_sq != nullptr) {
+      // The 32 lanes of a warp hold 32 consecutive groups: one 128-column
+      // block of row r (SW is a multiple of 128).
+      sq = WarpSum(sq);
+      if (lane == 0 && r < rows) g.ep.row_sq[(row0 + r) * g.ep.row_sq_ld + col / 128] = sq;
     }
   }
   if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes

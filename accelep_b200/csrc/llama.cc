@@ -571,6 +571,7 @@ class Engine {
     moved |= logits.Ensure(S * cfg.vocab * 4);
     moved |= last_rows.Ensure(S * 4);
     moved |= seq_first.Ensure(S * 4);
+    moved |= row_sq.Ensure(static_cast<size_t>(S) * SqBlocks() * sizeof(double));
     moved |= seq_count.Ensure(S * 4);
     moved |= seq_pos0.Ensure(S * 4);
     moved |= lens.Ensure(S * 4);
@@ -626,10 +627,17 @@ class Engine {
 
   // RmsNorm(x) then the product (src/llama_model.cc:228-229, :237-238, :245-246):
   // one kernel for int8 weights; through `normed` for fp32 weights.
+  // With `sq` (decode, int8 weights) the rows' sums of squares come from the
+  // product that wrote x, so the norm reads 5 values per row, not the row.
   void NormGemm(const float* x, const DevBuf& gamma, const Group& g, int64_t m, float* c, int64_t ldc,
-                const accel_b200_epilogue* ep, DevBuf& normed_buf) {
+                const accel_b200_epilogue* ep, DevBuf& normed_buf, const double* sq = nullptr) {
     const int64_t H = cfg.hidden;
-    if (g.kind == WKind::Q8) {
+    if (g.kind == WKind::Q8 && sq != nullptr) {
+      accel_b200_q8_plane plane{g.w.as<int8_t>(), g.scale.as<float>(), nullptr, 0, 1};
+      Abi(accel_b200_matmul_q8_rmsnorm_stats(x, H, sq, SqBlocks(), static_cast<int32_t>(SqBlocks()),
+                                             gamma.as<float>(), cfg.eps, &plane, c, ldc, m, g.k, g.n, ep, gemm_ws.p,
+                                             gemm_ws.bytes, stream));
+    } else if (g.kind == WKind::Q8) {
       accel_b200_q8_plane plane{g.w.as<int8_t>(), g.scale.as<float>(), nullptr, 0, 1};
       Abi(accel_b200_matmul_q8_rmsnorm(x, H, gamma.as<float>(), cfg.eps, &plane, c, ldc, m, g.k, g.n, ep, gemm_ws.p,
                                        gemm_ws.bytes, stream));
@@ -637,6 +645,20 @@ class Engine {
       Abi(accel_b200_rmsnorm(x, gamma.as<float>(), normed_buf.as<float>(), m, H, cfg.eps, 0, stream));
       Gemm(normed_buf.as<float>(), H, g, m, c, ldc, ep);
     }
+  }
+
+  // 128-column blocks of a hidden row (one sum of squares each).
+  int64_t SqBlocks() const { return (cfg.hidden + 127) / 128; }
+
+  // Whether every product that writes or normalizes the hidden rows runs on
+  // int8 weights (the GEMV and tensor-core kernels write row sums of squares).
+  bool AllQ8() const {
+    for (const Layer& l : layers) {
+      if (l.qkv.kind != WKind::Q8 || l.o.kind != WKind::Q8 || l.gu.kind != WKind::Q8 || l.down.kind != WKind::Q8) {
+        return false;
+      }
+    }
+    return true;
   }
 
   // src/llama_model.cc:209-247 over `rows` rows of `seqs` sequences. The
@@ -658,12 +680,20 @@ class Engine {
     residual.alpha = 1.f;
     residual.residual = hid;
     residual.residual_ld = H;
+    // Decode on int8 weights: the o and down products also write each hidden
+    // row's sums of squares, which the next RmsNorm-fed product reads.
+    const double* sq = nullptr;
+    if (decode && AllQ8()) {
+      residual.row_sq = row_sq.as<double>();
+      residual.row_sq_ld = SqBlocks();
+      sq = row_sq.as<double>();
+    }
     Abi(accel_b200_embed(tok, 0, embed.as<float>(), hid, rows, H, cfg.vocab, nullptr, stream));
     for (int32_t li = 0; li < cfg.layers; ++li) {
       Layer& l = layers[static_cast<size_t>(li)];
       float* kc = k_cache[static_cast<size_t>(li)].as<float>();
       float* vc = v_cache[static_cast<size_t>(li)].as<float>();
-      NormGemm(hid, l.attn_norm, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr, normed);
+      NormGemm(hid, l.attn_norm, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr, normed, li > 0 ? sq : nullptr);
       if (decode && head_dim == 64) {
         // Rope, AppendCache and attention of the new rows in one kernel.
         Abi(accel_b200_decode_attention(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
@@ -685,7 +715,7 @@ class Engine {
         }
       }
       Gemm(mixed.as<float>(), q_out, l.o, rows, hid, H, &residual);
-      NormGemm(hid, l.post_norm, l.gu, rows, gu.as<float>(), 2 * I, nullptr, normed);
+      NormGemm(hid, l.post_norm, l.gu, rows, gu.as<float>(), 2 * I, nullptr, normed, sq);
       if (l.down.kind == WKind::Q8) {
         // SiluMul feeds the down projection's operand directly.
         accel_b200_q8_plane plane{l.down.w.as<int8_t>(), l.down.scale.as<float>(), nullptr, 0, 1};
@@ -761,6 +791,7 @@ class Engine {
   DevBuf tokens, row_seq, row_pos, last_rows, lens, dec_seq, dec_pos, done, count, pre_ids, rng, step, finished;
   // Prefill rows by sequence: first row, row count and first position.
   DevBuf seq_first, seq_count, seq_pos0;
+  DevBuf row_sq;  // decode: per hidden row, sums of squares of its 128-column blocks
   int32_t prefill_max_rows = 0;
   DevBuf ids;
   int32_t ids_rows = 0;

@@ -105,7 +105,9 @@ def gemm_epilogue(c, alpha, bias, bias_shape, beta, act):
     return c
 
 
-def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none", residual=None):
+def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none", residual=None, row_sq=None):
+    """row_sq: a float64 [m, ceil(n / 128)] tensor that receives each row's
+    sums of squares of the outputs per 128-column block."""
     ep = Epilogue()
     ep.alpha, ep.beta = alpha, beta
     ep.bias = 0 if bias is None else bias.data_ptr()
@@ -113,8 +115,10 @@ def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none
     ep.act = ACT[act]
     ep.residual = 0 if residual is None else residual.data_ptr()
     ep.residual_ld = 0 if residual is None else residual.stride(0)
+    ep.row_sq = 0 if row_sq is None else row_sq.data_ptr()
+    ep.row_sq_ld = 0 if row_sq is None else row_sq.stride(0)
     # The struct holds raw addresses: keep the tensors alive with it.
-    ep._keep = (bias, residual)
+    ep._keep = (bias, residual, row_sq)
     return ep
 
 
@@ -192,6 +196,23 @@ def matmul_q8_rmsnorm(x, gamma, eps, q, scale, axis=1, epilogue=None, out=None, 
     check(lib.accel_b200_matmul_q8_rmsnorm(_p(x), x.stride(0), _p(gamma), eps, ctypes.byref(plane), _p(c), c.stride(0),
                                            m, k, n, None if epilogue is None else ctypes.byref(epilogue), _p(ws),
                                            0 if ws is None else ws.numel(), _s()))
+    return c
+
+
+def matmul_q8_rmsnorm_stats(x, row_sq, gamma, eps, q, scale, axis=1, epilogue=None, out=None, workspace=None):
+    """RmsNorm(x[:, :k]) @ dequant(q) with each row's sum of squares given as
+    row_sq [m, blocks] (float64 partial sums, added in order)."""
+    lib = load()
+    m = x.shape[0]
+    k, n = q.shape
+    c = out if out is not None else torch.zeros(m, n, dtype=torch.float32, device=x.device)
+    plane = Q8Plane(q.data_ptr(), scale.data_ptr(), 0, 0, axis)
+    need = lib.accel_b200_matmul_q8_rmsnorm_workspace(m, k, n)
+    ws = workspace if workspace is not None else _workspace(x.device, need)
+    check(lib.accel_b200_matmul_q8_rmsnorm_stats(_p(x), x.stride(0), _p(row_sq), row_sq.stride(0), row_sq.shape[1],
+                                                 _p(gamma), eps, ctypes.byref(plane), _p(c), c.stride(0), m, k, n,
+                                                 None if epilogue is None else ctypes.byref(epilogue), _p(ws),
+                                                 0 if ws is None else ws.numel(), _s()))
     return c
 
 

@@ -151,6 +151,15 @@ typedef struct accel_b200_epilogue {
   int32_t act;
   const float* residual;
   int64_t residual_ld;
+  /* Optional (NULL: none), int8 products on the GEMV and tensor-core paths:
+     for each output row r and each 128-column block t of the output, the sum
+     of squares of the final output values (in double; the four values a lane
+     holds in order, then a butterfly over the block's 32 lanes) is written to
+     row_sq[r * row_sq_ld + t], row_sq_ld >= ceil(n / 128). A following
+     RmsNorm-fed product reads these sums instead of the rows
+     (accel_b200_matmul_q8_rmsnorm_stats). */
+  double* row_sq;
+  int64_t row_sq_ld;
 } accel_b200_epilogue;
 
 /* Scratch, in bytes, accel_b200_matmul_q8 needs for these sizes. */
@@ -231,6 +240,18 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
    accel_b200_matmul_q8_rmsnorm_workspace(m, k, n) bytes whose first 64 KiB
    are zero. */
 ACCEL_B200_API size_t accel_b200_matmul_q8_rmsnorm_workspace(int64_t m, int64_t k, int64_t n);
+/* The same with each row's sum of squares supplied by the kernel that wrote
+   x (accel_b200_epilogue.row_sq): row_sq[r * row_sq_ld + t], t < row_sq_n,
+   added in order, replaces reading the whole row. No reference counterpart
+   (the norm itself is src/sim_rmsnorm.cc:7-20). The normalized values equal
+   accel_b200_matmul_q8_rmsnorm's up to the last bit of the double sum of
+   squares (another summation order). Where the planes pass runs (m > 64 or
+   long K) the rows are read as in accel_b200_matmul_q8_rmsnorm. */
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm_stats(const float* x, int64_t ldx, const double* row_sq,
+                                                      int64_t row_sq_ld, int32_t row_sq_n, const float* gamma,
+                                                      float eps, const accel_b200_q8_plane* b, float* c, int64_t ldc,
+                                                      int64_t m, int64_t k, int64_t n, const accel_b200_epilogue* ep,
+                                                      void* workspace, size_t workspace_bytes, void* stream);
 ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, const float* gamma, float eps,
                                                 const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
                                                 int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,

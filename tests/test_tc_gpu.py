@@ -136,3 +136,41 @@ def test_rmsnorm_product(lib, cuda, orc, m, k, n, ldx):
     dev_normed = K.rmsnorm(xt[:, :k].contiguous(), gt, m, k, 1e-5)
     two_step = H(K.matmul_q8(dev_normed, wt, st, epilogue=K.make_epilogue(act="relu")))
     assert np.array_equal(got, two_step)
+
+
+@pytest.mark.parametrize("m,k,n,path", [(32, 576, 576, 2), (32, 1536, 576, 2), (200, 576, 576, 2), (4, 576, 576, 3),
+                                        (1, 1536, 1000, 3)])
+def test_row_sums_of_squares(lib, cuda, m, k, n, path):
+    """accel_b200_epilogue.row_sq on the tensor-core (split and unsplit K) and
+    GEMV paths: per row and 128-column block, the sum of squares of the final
+    outputs (after the residual), against numpy's sum in float64."""
+    K.set_q8_path(path)
+    x, w, s = syn.int8_gemm(m, k, n, m + k + n)
+    res = T(np.random.default_rng(m).standard_normal((m, n), dtype=np.float32))
+    blocks = (n + 127) // 128
+    sq = torch.full((m, blocks + 1), -1.0, dtype=torch.float64, device="cuda")
+    out = H(K.matmul_q8(T(x), T(w), T(s), epilogue=K.make_epilogue(residual=res, row_sq=sq)))
+    got = H(sq)
+    o = out.astype(np.float64)
+    want = np.stack([(o[:, b * 128:(b + 1) * 128] ** 2).sum(axis=1) for b in range(blocks)], axis=1)
+    np.testing.assert_allclose(got[:, :blocks], want, rtol=1e-12)
+    assert (got[:, blocks] == -1.0).all()  # nothing written past the blocks
+
+
+def test_rmsnorm_from_sums_of_squares(lib, cuda, orc):
+    """The RmsNorm-fed product with the row sums of squares supplied (as the
+    engine's decode chains them: the residual product writes them, the next
+    product reads them) against the row-reading form."""
+    m, h, n = 32, 576, 960
+    rng = np.random.default_rng(3)
+    xs, w1, s1 = syn.int8_gemm(m, h, h, 5)
+    resid = T(rng.standard_normal((m, h), dtype=np.float32))
+    sq = torch.zeros(m, 5, dtype=torch.float64, device="cuda")
+    hid = K.matmul_q8(T(xs), T(w1), T(s1), epilogue=K.make_epilogue(residual=resid, row_sq=sq))
+    gamma = T(rng.uniform(0.5, 1.5, h).astype(np.float32))
+    _, w2, s2 = syn.int8_gemm(1, h, n, 6)
+    by_rows = H(K.matmul_q8_rmsnorm(hid, gamma, 1e-5, T(w2), T(s2)))
+    by_sums = H(K.matmul_q8_rmsnorm_stats(hid, sq, gamma, 1e-5, T(w2), T(s2)))
+    np.testing.assert_allclose(by_sums, by_rows, rtol=1e-6, atol=1e-6)
+    want = orc.execute_matmul_q(orc.rmsnorm(H(hid), H(gamma), m, h, 1e-5), w2, s2)
+    np.testing.assert_allclose(by_sums, want, rtol=1e-4, atol=1e-4)
