@@ -412,6 +412,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // The first weight blocks (one per conversion buffer) are converted before
+    // anything waits for the activations: the weights are immutable, so this
+    // overlaps the previous kernel, and after the activations land only the
+    // split stands between them and the MMA.
+    const int pre = min(kConvBufs, nkb);
+    for (int i = 0; i < pre; ++i) {
+      ok &= MbarWait(&full_w[i % S], (i / S) & 1);
+      ConvertWeightBlock(smem + (i % S) * L::kStage + L::kXBytes, conv_base + i * kWConv, ct);
+    }
     if constexpr (M == kANorm) {
       // Row RMS of the valid rows: from the producer's sums of squares when
       // given, else from the whole rows of A.
@@ -431,9 +440,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S, c = i % kConvBufs;
       uint8_t* stage = smem + s * L::kStage;
-      ok &= MbarWait(&full_w[s], (i / S) & 1);
-      ok &= MbarWait(&cempty[c], ((i / kConvBufs) & 1) ^ 1);
-      ConvertWeightBlock(stage + L::kXBytes, conv_base + c * kWConv, ct);
+      if (i >= pre) {
+        ok &= MbarWait(&full_w[s], (i / S) & 1);
+        ok &= MbarWait(&cempty[c], ((i / kConvBufs) & 1) ^ 1);
+        ConvertWeightBlock(stage + L::kXBytes, conv_base + c * kWConv, ct);
+      }
       if constexpr (M != kAPlanes) {
         ok &= MbarWait(&full_x[s], (i / S) & 1);
         const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBk;
