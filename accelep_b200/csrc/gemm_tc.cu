@@ -511,13 +511,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (cta_ok && tid < cols) {
       const int64_t col = n0 + tid;
       const float sc = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
+      if (g.peers.n == 0 && g.ep.row_sq == nullptr) {
+        // The common case, kept free of the optional outputs (a loop over peers
+        // inside this loop measured 30% slower on prefill-sized tiles).
 #pragma unroll 4
-      for (int64_t r = 0; r < rows; ++r) {
-        const int64_t row = row0 + r;
-        const float o = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
-        g.c[row * g.ldc + col] = o;
-        StorePeers(g.peers, row * g.ldc + col, o);
-        if (g.ep.row_sq != nullptr) tile[r * kBn + tid] = o;
+        for (int64_t r = 0; r < rows; ++r) {
+          const int64_t row = row0 + r;
+          g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
+        }
+      } else {
+        for (int64_t r = 0; r < rows; ++r) {
+          const int64_t row = row0 + r;
+          const float o = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
+          g.c[row * g.ldc + col] = o;
+          StorePeers(g.peers, row * g.ldc + col, o);
+          if (g.ep.row_sq != nullptr) tile[r * kBn + tid] = o;
+        }
       }
     }
     if (g.peers.n > 0) __threadfence_system();
