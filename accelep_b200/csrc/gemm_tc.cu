@@ -606,11 +606,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         float o[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q);
+        if (g.ep.row_sq != nullptr) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (c4 + q < cols) {
-            const double dv = static_cast<double>(o[q]);
-            sq += dv * dv;
+          for (int q = 0; q < 4; ++q) {
+            if (c4 + q < cols) {
+              const double dv = static_cast<double>(o[q]);
+              sq += dv * dv;
+            }
           }
         }
         const int64_t off = row * g.ldc + n0 + c4;

@@ -227,11 +227,13 @@ __global__ void __launch_bounds__(kGvThreads) Q8GemvKernel(GemvArgs g) {
           }
         }
       }
+      if (g.ep.row_sq != nullptr) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (col + q < g.n) {
-          const double dv = static_cast<double>(o[q]);
-          sq += dv * dv;
+        for (int q = 0; q < 4; ++q) {
+          if (col + q < g.n) {
+            const double dv = static_cast<double>(o[q]);
+            sq += dv * dv;
+          }
         }
       }
     }
