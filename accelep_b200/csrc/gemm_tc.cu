@@ -128,6 +128,9 @@ __device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
+__device__ __forceinline__ void TmemLoadCols(uint32_t taddr, float (&v)[32]) { TmemLoad32(taddr, v); }
+__device__ __forceinline__ void TmemLoadCols(uint32_t taddr, float (&v)[16]) { TmemLoad16(taddr, v); }
+
 __device__ __forceinline__ uint32_t PackBf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -288,8 +291,9 @@ __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int6
   }
 }
 
+// R = 16 planes kernels (long weight streams, m <= 16) run three CTAs per SM.
 template <int R, int kStagesT, int M>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, (R == 16 && M == kAPlanes) ? 3 : 1)
     Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                    const __grid_constant__ CUtensorMap tu, TcArgs g) {
   using L = Tc<R, kStagesT, M>;
@@ -298,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // memory: one MMA with N = 3R covers all of them when 3R <= 256 and reads the
   // weight operand once; D column p * R + r then holds plane p of row r.
   constexpr bool kOneMma = 3 * R <= 256;
-  constexpr uint32_t kCols = 3 * R <= 128 ? 128 : (3 * R <= 256 ? 256 : 512);
+  constexpr uint32_t kCols = 3 * R <= 64 ? 64 : (3 * R <= 128 ? 128 : (3 * R <= 256 ? 256 : 512));
   constexpr uint32_t kIdesc = InstrDescBf16(kOneMma ? 3 * R : R, true);
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_w[kMaxStages], full_x[kMaxStages], empty[kMaxStages], cfull[kConvBufs],
@@ -482,25 +486,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp >= 2) {
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. +31
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    constexpr int kChunk = R < 32 ? R : 32;  // TMEM columns per load
 #pragma unroll 1
-    for (int c0 = 0; c0 < R; c0 += 32) {
-      float v[32];
+    for (int c0 = 0; c0 < R; c0 += kChunk) {
+      float v[kChunk];
       if (nkb > 0 && cta_ok) {
         // hi + mid + lo, each accumulated separately over K.
-        float w[32];
-        TmemLoad32(lane_base + c0, v);
-        TmemLoad32(lane_base + R + c0, w);
+        float w[kChunk];
+        TmemLoadCols(lane_base + c0, v);
+        TmemLoadCols(lane_base + R + c0, w);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += w[j];
-        TmemLoad32(lane_base + 2 * R + c0, w);
+        for (int j = 0; j < kChunk; ++j) v[j] += w[j];
+        TmemLoadCols(lane_base + 2 * R + c0, w);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += w[j];
+        for (int j = 0; j < kChunk; ++j) v[j] += w[j];
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = cta_ok ? 0.f : __int_as_float(0x7fc00000);
+        for (int j = 0; j < kChunk; ++j) v[j] = cta_ok ? 0.f : __int_as_float(0x7fc00000);
       }
 #pragma unroll
-      for (int j = 0; j < 32; ++j) tile[(c0 + j) * kBn + quarter * 32 + lane] = v[j];
+      for (int j = 0; j < kChunk; ++j) tile[(c0 + j) * kBn + quarter * 32 + lane] = v[j];
     }
   }
   TcFenceBeforeSync();
@@ -719,9 +724,12 @@ constexpr int MaxStages() {
   return stage * 4 + kConvBufs * kWConv + 1024 <= 227 * 1024 ? 4 : 3;
 }
 
+// Activation rows per tile (the MMA's N is three times this).
+int64_t TileRows(int64_t m) { return m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128)); }
+
 TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   TcPlan p{};
-  p.r = m <= 32 ? 32 : (m <= 64 ? 64 : 128);
+  p.r = static_cast<int>(TileRows(m));
   p.feature_tiles = CeilDiv(n, kBn);
   p.row_tiles = CeilDiv(m, p.r);
   p.kb_total = static_cast<int32_t>(CeilDiv(k, kBk));
@@ -731,12 +739,14 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   const int64_t base = p.feature_tiles * p.row_tiles;
   int64_t splits = 1;
   if (base < kSms && p.kb_total > 1) {
-    splits = Min64(CeilDiv(p.kb_total, 2), CeilDiv(2 * kSms, base));
+    // R = 16 tiles run three CTAs per SM: the largest split whose grid fits
+    // in one wave of them.
+    splits = Min64(CeilDiv(p.kb_total, 2), p.r == 16 ? (3 * kSms) / base : CeilDiv(2 * kSms, base));
     if (splits > 8) splits = 8;
   }
   p.kb_per_split = static_cast<int32_t>(CeilDiv(p.kb_total, splits));
   p.splits = static_cast<int32_t>(CeilDiv(p.kb_total, p.kb_per_split));
-  p.stages = p.kb_per_split <= 2 ? 2 : 4;  // 4: as many as fit (MaxStages)
+  p.stages = p.kb_per_split <= 2 ? 2 : 4;  // 4: as many as fit (MaxStages, or fewer for more CTAs per SM)
   // Splitting fp32 tiles in the kernel saves the planes pass (one launch) but
   // adds converter work to every k block: worth it for CTAs that walk few
   // blocks (latency-bound decode products), not for long weight streams.
@@ -780,12 +790,26 @@ template <int R, int M>
 int LaunchTcStages(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
                    const TcPlan& p, cudaStream_t s) {
   if (p.stages == 2) return LaunchTc<R, 2, M>(tw, tx, tu, g, p, s);
-  // Long weight streams with few rows (planes mode, R = 32): three stages
-  // leave room for two CTAs per SM, doubling the converter warps per SM.
-  if constexpr (R == 32 && M == kAPlanes) {
+  // Long weight streams with few rows (planes mode): fewer stages leave room
+  // for more CTAs per SM, and so more converter warps per SM: two at R = 32
+  // with three stages, three at R = 16 with two.
+  if constexpr (R == 16 && M == kAPlanes) {
+    return LaunchTc<R, 2, M>(tw, tx, tu, g, p, s);
+  } else if constexpr (R == 32 && M == kAPlanes) {
     return LaunchTc<R, 3, M>(tw, tx, tu, g, p, s);
   } else {
     return LaunchTc<R, MaxStages<R, M>(), M>(tw, tx, tu, g, p, s);
+  }
+}
+
+// In-kernel split modes run at R <= 64 (the plan takes planes at R = 128).
+template <int M>
+int LaunchTcRows(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
+                 const TcPlan& p, cudaStream_t s) {
+  switch (p.r) {
+    case 16: return LaunchTcStages<16, M>(tw, tx, tu, g, p, s);
+    case 32: return LaunchTcStages<32, M>(tw, tx, tu, g, p, s);
+    default: return LaunchTcStages<64, M>(tw, tx, tu, g, p, s);
   }
 }
 
@@ -810,7 +834,7 @@ bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, cons
   if (m <= 0 || k <= 0 || n <= 0 || n % 16 != 0 || k % 8 != 0 || lda % 4 != 0) return false;
   if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0) return false;
   if (k > (int64_t{1} << 31) - 1 || n > (int64_t{1} << 31) - 1 || m > (int64_t{1} << 31) - 1) return false;
-  return CeilDiv(m, m <= 32 ? 32 : (m <= 64 ? 64 : 128)) <= 65535 && EncodeFn() != nullptr;
+  return CeilDiv(m, TileRows(m)) <= 65535 && EncodeFn() != nullptr;
 }
 
 size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
@@ -893,21 +917,15 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   }
   if (p.mode == kAPlanes) {
     switch (p.r) {
+      case 16: return LaunchTcStages<16, kAPlanes>(tw, tx, tu, g, p, stream);
       case 32: return LaunchTcStages<32, kAPlanes>(tw, tx, tu, g, p, stream);
       case 64: return LaunchTcStages<64, kAPlanes>(tw, tx, tu, g, p, stream);
       default: return LaunchTcStages<128, kAPlanes>(tw, tx, tu, g, p, stream);
     }
   }
-  if (p.mode == kASilu) {
-    return p.r == 32 ? LaunchTcStages<32, kASilu>(tw, tx, tu, g, p, stream)
-                     : LaunchTcStages<64, kASilu>(tw, tx, tu, g, p, stream);
-  }
-  if (p.mode == kANorm) {
-    return p.r == 32 ? LaunchTcStages<32, kANorm>(tw, tx, tu, g, p, stream)
-                     : LaunchTcStages<64, kANorm>(tw, tx, tu, g, p, stream);
-  }
-  return p.r == 32 ? LaunchTcStages<32, kAF32>(tw, tx, tu, g, p, stream)
-                   : LaunchTcStages<64, kAF32>(tw, tx, tu, g, p, stream);
+  if (p.mode == kASilu) return LaunchTcRows<kASilu>(tw, tx, tu, g, p, stream);
+  if (p.mode == kANorm) return LaunchTcRows<kANorm>(tw, tx, tu, g, p, stream);
+  return LaunchTcRows<kAF32>(tw, tx, tu, g, p, stream);
 }
 
 }  // namespace accel_b200

@@ -41,7 +41,7 @@ def tensor_cores():
 
 @pytest.mark.parametrize("m,k,n", [(1, 64, 128), (32, 576, 960), (7, 100, 336), (33, 576, 576), (64, 1536, 576),
                                    (100, 192, 3072), (130, 576, 1536), (300, 640, 272), (32, 1536, 49152),
-                                   (5, 4104, 256), (128, 8192, 512)])
+                                   (5, 4104, 256), (128, 8192, 512), (16, 16384, 16384), (12, 4096, 1024)])
 def test_tc_matches_checker(lib, cuda, orc, m, k, n):
     x, w, s = syn.int8_gemm(m, k, n, m + k + n)
     res = np.random.default_rng(m).standard_normal((m, n), dtype=np.float32)
@@ -103,12 +103,12 @@ def test_silu_product_matches_checker(lib, cuda, orc, m, inter, n):
 
 
 def test_fp32_tile_product_every_row_count(lib, cuda, orc):
-    """m = 1 .. 64 on the fp32-tile path (R = 32 and 64, ragged row tiles)."""
+    """m = 1 .. 64 on the fp32-tile path (R = 16, 32 and 64, ragged row tiles)."""
     x, w, s = syn.int8_gemm(64, 576, 256, 11)
     xt, wt, st = T(x), T(w), T(s)
     want = orc.execute_matmul_q(x, w, s)
     mag = np.abs(x).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
-    for m in (1, 2, 31, 32, 33, 63, 64):
+    for m in (1, 2, 15, 16, 17, 31, 32, 33, 63, 64):
         got = H(K.matmul_q8(xt[:m].contiguous(), wt, st))
         check_close(got, want[:m], 576, mag[:m])
 
