@@ -4,37 +4,54 @@
 // [k, n] (n contiguous: the reference's QuantPlane layout) and a per-column
 // (or single) scale: src/sim_device.cc:541-602 and the epilogue of
 // src/runtime.cc:332-344. A may also be SiluMul of a fused gate|up row
-// (src/sim_silu.cc:8-13 then the down projection, src/llama_model.cc:239-240).
+// (src/sim_silu.cc:8-13 then the down projection, src/llama_model.cc:239-240)
+// or RmsNorm of a row (src/sim_rmsnorm.cc, then the q|k|v, gate|up and LM-head
+// products of src/llama_model.cc).
 //
-// Arithmetic. int8 -> bf16 is exact (|q| <= 128 needs 8 significant bits).
-// Each fp32 activation is split into three bf16 planes hi + mid + lo (each the
-// rounded remainder of the previous); together they carry the 24-bit fp32
-// significand, every product with the bf16 weight is exact, and the planes
-// accumulate separately in fp32 in TMEM. The MMA is issued "swapped": M = 128
-// runs over output features and N over activation rows (all three planes in
-// one MMA of N = 3R when 3R <= 256), so decode with 32 rows is a full-width MMA.
+// Arithmetic: exact integer dot products. The weights stay int8: TMA writes
+// the raw block with 128-byte swizzle, which is the MMA's MN-major canonical
+// layout, and kind::i8 MMAs consume it directly (no conversion). Each
+// activation row segment (the k range one CTA of a split-K cluster walks; the
+// whole row without a split) is put in 30-bit fixed point against its largest
+// magnitude: with e the
+// smallest exponent such that every |y| < 2^e, X = rint(y * 2^(30 - e)), so an
+// element keeps 24 significant bits when |y| >= 2^(e - 7) and an absolute error
+// of at most 2^(e - 31) otherwise. X is written as four balanced base-256 digits
+// (int8, X = d0 2^24 + d1 2^16 + d2 2^8 + d3), the four digit planes are the
+// MMA's B operand, and the tensor core sums w * d exactly in int32 (|sum| <
+// 2^31 for up to 2^17 k per CTA). The epilogue recombines the planes in int64,
+// rounds once to fp32 and scales by 2^(e - 30): the result is the correctly
+// rounded dot product of the weights with the fixed-point row, which is no
+// further from the exact product than the reference's own fp32 accumulation.
+// A row holding Inf or NaN yields NaN outputs.
+//
+// The MMA is issued "swapped": M = 128 runs over output features and N over
+// activation rows times digit planes (N = 4R; two MMAs of N = 256 at R = 128),
+// so decode with 32 rows is a full-width MMA.
 //
 // Activation operand, by mode:
-//   planes  (m > 64): a separate pass writes the three planes [3][m][k] to the
-//           workspace; TMA loads them with 128-byte swizzle, which is already
-//           the MMA's K-major canonical layout.
-//   fp32    (m <= 64): TMA loads the fp32 tile [R rows x 64 k]; the converter
-//           warps split it into the planes in shared memory.
-//   silu    (m <= 64): TMA loads the gate and up tiles; the converter warps form
-//           silu(g) * u exactly as SiluMul rounds it and split the result.
+//   planes  (R = 128, or more than two k blocks per CTA): a separate pass
+//           forms each row segment (plain, SiluMul or RmsNorm), finds its
+//           exponent and writes the digit planes [4][m][kp] and the exponents
+//           [segments][m] to the workspace; TMA loads [4][R][128 k] tiles with
+//           128-byte swizzle, already the MMA's K-major canonical layout.
+//   in-kernel (up to two k blocks per CTA, R <= 64): TMA loads the CTA's fp32
+//           tiles [R rows x 128 k] (gate and up for SiluMul); the converter
+//           warps form them (SiluMul exactly as SiluMul rounds it, RmsNorm
+//           exactly as RmsNormKernel rounds it), find the exponents over the
+//           range and write the digit planes into shared memory.
 //
-// Pipeline (one CTA = one 128-feature x R-row tile over a range of 64-deep k
-// blocks; 6 warps):
-//   warp 0  producer: per k block one TMA of the raw int8 weight block
-//           [64 k x 128 n] and the activation load(s) of the mode; a ring of
-//           stages.
-//   warps 2-5 converters: int8 -> bf16 (integer and fp32-add bit arithmetic,
-//           exact) into the MMA's n-contiguous swizzled layout (two buffers),
-//           and the split of fp32 activations; afterwards the epilogue:
-//           tcgen05.ld of the accumulator into a shared tile, then scale,
-//           fused epilogue and coalesced row stores.
-//   warp 1  MMA issuer (one thread): 4 k steps per block, then tcgen05.commit
-//           to the barriers that free the stage and the buffer.
+// Pipeline (one CTA = one 128-feature x R-row tile over a range of 128-deep k
+// blocks; 6 or 10 warps):
+//   warp 0  producer: per k block one TMA of the int8 weight block [128 k x
+//           128 n] and one of the digit tile (planes) or the fp32 tile(s)
+//           (in-kernel); a ring of stages.
+//   warp 1  MMA issuer (one thread): 4 k steps of 32 per block, then
+//           tcgen05.commit to the barrier that frees the stage.
+//   warps 2.. converters (eight in-kernel, four in planes mode): the
+//           in-kernel operand, then the epilogue: tcgen05.ld of the
+//           accumulators into a shared fp32 tile, then scale, fused epilogue
+//           and coalesced row stores.
 // K can be split across the CTAs of one thread-block cluster (up to 8); each
 // keeps its partial tile in shared memory and the cluster sums the tiles in
 // rank order through distributed shared memory, so the result is
@@ -46,7 +63,6 @@
 // touched after it. Every mbarrier wait is bounded (tma.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
-#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -63,41 +79,51 @@ namespace accel_b200 {
 
 namespace {
 
-constexpr int kBk = 64;                // k per block: 128 bytes of bf16, one swizzle row
-constexpr int kBn = 128;               // output features per tile (MMA M)
-constexpr int kMmaK = 16;              // k per bf16 MMA
-constexpr int kWRaw = kBk * kBn;       // raw int8 weight block, 8 KiB
-constexpr int kWConv = kBk * kBn * 2;  // converted bf16 weight block, 16 KiB
-constexpr int kConvBufs = 2;
-constexpr int kConvWarps = 4;
-constexpr int kThreads = (2 + kConvWarps) * 32;
-constexpr int kMaxStages = 4;
+constexpr int kBk = 128;                // k per block: one 128-byte swizzle row of int8
+constexpr int kBn = 128;                // output features per tile (MMA M)
+constexpr int kMmaK = 32;               // k per int8 MMA
+constexpr int kWBytes = kBk * kBn;      // int8 weight block, 16 KiB
+constexpr int kDigits = 4;              // int8 digits per fixed-point activation
+constexpr int kExpMin = -96;            // smallest row exponent: keeps 2^(30 - e) a normal float
+constexpr int32_t kBadRow = 0x7fff;     // exponent of a row holding Inf or NaN
+constexpr int kMaxBlocksPerCta = 1024;  // 2^17 k: int32 sums of int8 x int8 cannot overflow
+constexpr int kInKernelBlocks = 2;      // k blocks of a CTA that forms its own operand
+// Converter warps: eight where they form the operand (latency-bound decode
+// products: more threads shorten the operand and epilogue work), four in
+// planes mode (long weight streams; R = 16 runs three CTAs per SM).
+template <int M>
+constexpr int ConvWarps() { return M == 0 ? 4 : 8; }
+template <int M>
+constexpr int Threads() { return (2 + ConvWarps<M>()) * 32; }
 
 enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2, kANorm = 3 };
 
 template <int R, int S, int M>
 struct Tc {
-  static constexpr int kXBytes = 3 * R * kBk * 2;  // three bf16 planes (MMA operand)
-  static constexpr int kXRaw = M == kAPlanes ? 0 : (M == kASilu ? 2 : 1) * R * kBk * 4;  // fp32 tiles
-  static constexpr int kXLoad = M == kAPlanes ? kXBytes : kXRaw;  // bytes the activation TMA delivers
-  static constexpr int kStage = kXBytes + kWRaw + kXRaw;          // planes first: 1024-aligned
+  static constexpr int kXBytes = kDigits * R * kBk;  // digit planes of one k block (MMA B operand)
+  static constexpr int kStage = kXBytes + kWBytes;   // digits, then the weight block; 1024-aligned
   static constexpr int kStages = S;
-  static constexpr int kTile = R * kBn * 4;  // fp32 accumulator tile, staged in stage memory
-  static constexpr int kStageArea = kStages * kStage > kTile ? kStages * kStage : kTile;
-  static constexpr int kSmem = kStageArea + kConvBufs * kWConv + 1024;
-  static_assert(kStages <= kMaxStages, "stage count");
+  static constexpr int kYTiles = M == kAPlanes ? 0 : (M == kASilu ? 2 : 1);  // fp32 tiles per k block
+  static constexpr int kYTile = R * kBk * 4;                                  // one fp32 tile [R][128 k]
+  static constexpr int kYBytes = kYTiles * kInKernelBlocks * kYTile;
+  static constexpr int kTile = R * kBn * 4;  // fp32 accumulator tile, over the stages after the main loop
+  static constexpr int kArea = S * kStage + kYBytes;
+  static constexpr int kSmem = (kArea > kTile ? kArea : kTile) + 1024;
+  static_assert(M == kAPlanes || S == kInKernelBlocks, "in-kernel operand: one stage per k block");
   static_assert(kStage % 1024 == 0, "stage alignment");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 struct TcArgs {
   const float* a;      // fp32 A rows (norm mode: the whole rows are read for their RMS)
+  const float* up;     // silu mode: the up rows (row stride lda)
   int64_t lda;
   const float* gamma;  // norm mode: RmsNorm weights [k]
   float eps;
   const double* sq_in;  // norm mode, optional: per row, sq_n partial sums of squares (stride sq_ld)
   int64_t sq_ld;
   int32_t sq_n;
+  const int32_t* row_exp;  // planes mode: [segment (grid y)][m] fixed-point exponents
   int64_t m, k, n;
   int32_t kb_total;
   int32_t kb_per_split;
@@ -128,113 +154,65 @@ __device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
-__device__ __forceinline__ void TmemLoadCols(uint32_t taddr, float (&v)[32]) { TmemLoad32(taddr, v); }
-__device__ __forceinline__ void TmemLoadCols(uint32_t taddr, float (&v)[16]) { TmemLoad16(taddr, v); }
-
-__device__ __forceinline__ uint32_t PackBf16(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-// Four int8 in a word -> two bf16x2 words, exactly and with full-rate integer
-// and fp32 adds only: XOR 0x80 turns each byte into q + 128 (offset binary);
-// a byte permute places it under the fp32 exponent of 2^23, so the float is
-// 2^23 + 128 + q; subtracting 2^23 + 128 leaves q exactly, and an integer-valued
-// float of at most 8 significant bits has a zero low half, so its top 16 bits
-// are the bf16 encoding.
-__device__ __forceinline__ void Int8x4ToBf16(uint32_t w, uint32_t* lo, uint32_t* hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
-  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
-  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
-  *lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-  *hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
-}
-
-// Raw weight block [64 k][128 n] int8 (dense rows of 128 bytes) -> bf16 in the
-// n-contiguous 128-byte-swizzled layout: atom (k / 8, n / 64) of 8 k rows x 128
-// bytes at (k / 8) * 2048 + (n / 64) * 1024; 16-byte chunk (n % 64) / 8 of row
-// k % 8 stored at chunk ^ (k % 8).
-__device__ __forceinline__ void ConvertWeightBlock(const uint8_t* raw, uint8_t* conv, int ct) {
-#pragma unroll
-  for (int pass = 0; pass < 4; ++pass) {
-    const int idx = pass * (kConvWarps * 32) + ct;
-    const int kl = idx >> 3;
-    const int nl = (idx & 7) * 16;
-    const uint4 q = *reinterpret_cast<const uint4*>(raw + kl * kBn + nl);
-    uint32_t p[8];
-    Int8x4ToBf16(q.x, &p[0], &p[1]);
-    Int8x4ToBf16(q.y, &p[2], &p[3]);
-    Int8x4ToBf16(q.z, &p[4], &p[5]);
-    Int8x4ToBf16(q.w, &p[6], &p[7]);
-    const int row = kl & 7;
-    uint8_t* atom = conv + (kl >> 3) * 2048 + (nl >> 6) * 1024 + row * 128;
-    const int chunk = (nl & 63) >> 3;
-    *reinterpret_cast<uint4*>(atom + ((chunk ^ row) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
-    *reinterpret_cast<uint4*>(atom + (((chunk + 1) ^ row) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
-  }
-}
-
-// hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid).
-__device__ __forceinline__ void Split3(float x, float* hi, float* mid, float* lo) {
-  *hi = __bfloat162float(__float2bfloat16_rn(x));
-  const float r1 = x - *hi;
-  *mid = __bfloat162float(__float2bfloat16_rn(r1));
-  *lo = r1 - *mid;
-}
-
 // SiluMul of one element as src/sim_silu.cc:8-13 rounds it.
 __device__ __forceinline__ float SiluMul(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
 }
 
-// fp32 activation tile(s) [R rows][64 k] (rows of 256 bytes) -> the three bf16
-// planes in the K-major 128-byte-swizzled layout the planes TMA would write:
-// plane p, row r at p * R * 128 + r * 128, 16-byte chunk j stored at
-// j ^ (r % 8). Each thread takes four consecutive k of one row per pass.
-// Rows at or past `valid` are skipped: their planes stay zero. Norm mode: the
-// element is RmsNorm'd first, float(double(x) * inv[row]) * gamma[k], as
-// RmsNormKernel rounds it (gamma points at this block's first k; `kvalid` k
-// of the block lie inside the matrix).
-template <int R, int M>
-__device__ __forceinline__ void SplitTile(const uint8_t* raw, uint8_t* planes, int ct, int valid,
-                                          const float* gamma, int kvalid, const double* inv) {
-#pragma unroll
-  for (int pass = 0; pass < R * 16 / (kConvWarps * 32); ++pass) {
-    const int idx = pass * (kConvWarps * 32) + ct;
-    const int row = idx >> 4, k4 = idx & 15;
-    if (pass * (kConvWarps * 32) >= valid * 16) break;  // uniform across the CTA
-    if (row >= valid) continue;
-    float x[4];
-    const float4 v = *reinterpret_cast<const float4*>(raw + row * 256 + k4 * 16);
-    if constexpr (M == kASilu) {
-      const float4 u = *reinterpret_cast<const float4*>(raw + R * 256 + row * 256 + k4 * 16);
-      x[0] = SiluMul(v.x, u.x);
-      x[1] = SiluMul(v.y, u.y);
-      x[2] = SiluMul(v.z, u.z);
-      x[3] = SiluMul(v.w, u.w);
-    } else if constexpr (M == kANorm) {
-      const float4 w = k4 * 4 < kvalid ? __ldg(reinterpret_cast<const float4*>(gamma + k4 * 4))
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      const double iv = inv[row];
-      x[0] = __fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), w.x);
-      x[1] = __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), w.y);
-      x[2] = __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), w.z);
-      x[3] = __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), w.w);
-    } else {
-      x[0] = v.x;
-      x[1] = v.y;
-      x[2] = v.z;
-      x[3] = v.w;
-    }
-    float h[4], md[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) Split3(x[j], &h[j], &md[j], &lo[j]);
-    const int off = row * 128 + (((k4 >> 1) ^ (row & 7)) << 4) + (k4 & 1) * 8;
-    *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(h[0], h[1]), PackBf16(h[2], h[3]));
-    *reinterpret_cast<uint2*>(planes + R * 128 + off) = make_uint2(PackBf16(md[0], md[1]), PackBf16(md[2], md[3]));
-    *reinterpret_cast<uint2*>(planes + 2 * R * 128 + off) = make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+// ------------------------------------------------------------ fixed point
+
+// Largest |y| of four values as float bits: unsigned order is magnitude order
+// for non-negative floats, and Inf and NaN order above every finite value.
+__device__ __forceinline__ uint32_t AbsMaxBits(float4 y) {
+  const uint32_t a = __float_as_uint(y.x) & 0x7fffffffu, b = __float_as_uint(y.y) & 0x7fffffffu;
+  const uint32_t c = __float_as_uint(y.z) & 0x7fffffffu, d = __float_as_uint(y.w) & 0x7fffffffu;
+  return max(max(a, b), max(c, d));
+}
+
+// The exponent e of a row whose largest |y| has float bits `amax`: every |y|
+// < 2^e (e >= kExpMin), or kBadRow when the row holds Inf or NaN.
+__device__ __forceinline__ int32_t RowExponent(uint32_t amax) {
+  if (amax >= 0x7f800000u) return kBadRow;
+  const int32_t e = static_cast<int32_t>(amax >> 23) - 126;
+  return e < kExpMin ? kExpMin : e;
+}
+
+// 2^(30 - e) as a float (exact: 30 - e lies in [-98, 126]).
+__device__ __forceinline__ float FixScale(int32_t e) { return __int_as_float((127 + 30 - e) << 23); }
+
+// The digit planes of four consecutive elements: word p holds digit p of the
+// four fixed-point values, byte i for element i. For one value, (X + 0x808080)
+// carries the balanced form's carries into bytes 1 .. 3, so XOR 0x808080 of it
+// holds the digits [d3, d2, d1, d0] in bytes 0 .. 3 (d3 = X mod 256 read as a
+// signed byte); a 4 x 4 byte transpose then gathers each digit's bytes.
+__device__ __forceinline__ void FourDigits(float4 y, float s, uint32_t (&w)[kDigits]) {
+  const auto word = [s](float v) {
+    return (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v, s))) + 0x808080u) ^ 0x808080u;
+  };
+  const uint32_t v0 = word(y.x), v1 = word(y.y), v2 = word(y.z), v3 = word(y.w);
+  const uint32_t t0 = __byte_perm(v0, v1, 0x5140), t1 = __byte_perm(v0, v1, 0x7362);  // bytes 0,1 | 2,3 of v0, v1
+  const uint32_t t2 = __byte_perm(v2, v3, 0x5140), t3 = __byte_perm(v2, v3, 0x7362);
+  w[3] = __byte_perm(t0, t2, 0x5410);
+  w[2] = __byte_perm(t0, t2, 0x7632);
+  w[1] = __byte_perm(t1, t3, 0x5410);
+  w[0] = __byte_perm(t1, t3, 0x7632);
+}
+
+// Element quad q (k = 4q .. 4q + 3) of a row as the mode forms it.
+template <int M>
+__device__ __forceinline__ float4 FormQuad(const float* a, const float* up, const float* gamma, double inv, int64_t q) {
+  const float4 v = __ldg(reinterpret_cast<const float4*>(a) + q);
+  if constexpr (M == kASilu) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(up) + q);
+    return make_float4(SiluMul(v.x, u.x), SiluMul(v.y, u.y), SiluMul(v.z, u.z), SiluMul(v.w, u.w));
+  } else if constexpr (M == kANorm) {
+    const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + q);
+    return make_float4(__fmul_rn(static_cast<float>(static_cast<double>(v.x) * inv), g.x),
+                       __fmul_rn(static_cast<float>(static_cast<double>(v.y) * inv), g.y),
+                       __fmul_rn(static_cast<float>(static_cast<double>(v.z) * inv), g.z),
+                       __fmul_rn(static_cast<float>(static_cast<double>(v.w) * inv), g.w));
+  } else {
+    return v;
   }
 }
 
@@ -259,10 +237,10 @@ __device__ __forceinline__ double RowInverseRms(const float* in, int64_t dim, fl
 // order, which is exact-commutative). Here thread q holds the partials of
 // lanes 8q .. 8q + 7, so levels 16 and 8 are shuffles with threads q ^ 2 and
 // q ^ 1 and levels 4, 2, 1 stay inside the thread. dim % 8 == 0.
-template <int R>
+template <int R, int CW>
 __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int64_t row0, int valid, int64_t dim,
                                                float eps, int ct, double* inv) {
-  for (int base = 0; base < R; base += kConvWarps * 8) {
+  for (int base = 0; base < R; base += CW * 8) {
     const int r = base + (ct >> 2), q = ct & 3;
     double s[8];
 #pragma unroll
@@ -291,28 +269,89 @@ __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int6
   }
 }
 
+// In-kernel operand: the fp32 tiles of the CTA's k blocks (block b at
+// ytiles + b * tiles * R * 128 floats: A, then up for SiluMul; rows of 128 k;
+// rows past the matrix and k past K read as zero) are formed as the mode does
+// (in place), the exponents over the range found (exp_s, every row of the
+// tile), and the digit planes of block b written into stage b: plane p, row r
+// at (p R + r) * 128, the 16-byte chunk j of a row stored at j ^ (r % 8) (the
+// TMA's 128-byte swizzle). Converter warp w takes block w % nkb, rows w / nkb,
+// + CW / nkb, ...; lane l the quad k = 4l .. 4l + 3 of the block.
+template <int R, int M, int CW>
+__device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0, const double* inv, float* ytiles,
+                                            uint32_t* amax, int32_t* exp_s, uint8_t* stages, int stage_bytes,
+                                            int ct) {
+  constexpr int kTiles = M == kASilu ? 2 : 1;
+  const int w = ct >> 5, lane = ct & 31;
+  const int b = w % nkb, r0 = w / nkb, rstep = CW / nkb;
+  const int kb = 4 * lane;  // k offset inside the block
+  float* y_at = ytiles + b * kTiles * R * kBk + kb;
+  float4 gam = make_float4(0.f, 0.f, 0.f, 0.f);
+  if constexpr (M == kANorm) {
+    if (k0 + b * kBk + kb < g.k) gam = __ldg(reinterpret_cast<const float4*>(g.gamma + k0 + b * kBk + kb));
+  }
+#pragma unroll 4
+  for (int r = r0; r < R; r += rstep) {
+    float4* at = reinterpret_cast<float4*>(y_at + r * kBk);
+    const float4 v = *at;
+    float4 y = v;
+    if constexpr (M == kASilu) {
+      const float4 u = *reinterpret_cast<const float4*>(y_at + R * kBk + r * kBk);
+      y = make_float4(SiluMul(v.x, u.x), SiluMul(v.y, u.y), SiluMul(v.z, u.z), SiluMul(v.w, u.w));
+      *at = y;
+    } else if constexpr (M == kANorm) {
+      const double iv = inv[r];
+      y = make_float4(__fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), gam.x),
+                      __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), gam.y),
+                      __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), gam.z),
+                      __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), gam.w));
+      *at = y;
+    }
+    const uint32_t m = __reduce_max_sync(kFull, AbsMaxBits(y));
+    if (lane == 0) amax[2 * r + b] = m;
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");  // converter warps only
+  const auto row_exponent = [&](int r) {
+    return RowExponent(nkb > 1 ? max(amax[2 * r], amax[2 * r + 1]) : amax[2 * r]);
+  };
+  if (ct < R) exp_s[ct] = row_exponent(ct);
+  uint8_t* xs = stages + b * stage_bytes;
+  const int chunk = kb >> 4, byte = kb & 15;
+#pragma unroll 4
+  for (int r = r0; r < R; r += rstep) {
+    const int32_t e = row_exponent(r);
+    const float4 y = *reinterpret_cast<const float4*>(y_at + r * kBk);
+    uint32_t d[kDigits] = {0u, 0u, 0u, 0u};
+    if (e != kBadRow) FourDigits(y, FixScale(e), d);
+    const int off = (((chunk ^ (r & 7)) << 4) | byte) + r * kBk;
+#pragma unroll
+    for (int p = 0; p < kDigits; ++p) *reinterpret_cast<uint32_t*>(xs + p * R * kBk + off) = d[p];
+  }
+}
+
 // R = 16 planes kernels (long weight streams, m <= 16) run three CTAs per SM.
 template <int R, int kStagesT, int M>
-__global__ void __launch_bounds__(kThreads, (R == 16 && M == kAPlanes) ? 3 : 1)
+__global__ void __launch_bounds__(Threads<M>(), (R == 16 && M == kAPlanes) ? 3 : 1)
     Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                    const __grid_constant__ CUtensorMap tu, TcArgs g) {
   using L = Tc<R, kStagesT, M>;
   constexpr int S = L::kStages;
-  // The three activation planes are 3R consecutive K-major rows in shared
-  // memory: one MMA with N = 3R covers all of them when 3R <= 256 and reads the
-  // weight operand once; D column p * R + r then holds plane p of row r.
-  constexpr bool kOneMma = 3 * R <= 256;
-  constexpr uint32_t kCols = 3 * R <= 64 ? 64 : (3 * R <= 128 ? 128 : (3 * R <= 256 ? 256 : 512));
-  constexpr uint32_t kIdesc = InstrDescBf16(kOneMma ? 3 * R : R, true);
+  constexpr int kConvWarps = ConvWarps<M>();
+  constexpr int kThreads = Threads<M>();
+  constexpr int kN = kDigits * R;                 // MMA N over all digit planes
+  constexpr int kMmas = kN <= 256 ? 1 : 2;        // R = 128: two MMAs of N = 256
+  constexpr int kNMma = kN / kMmas;
+  constexpr uint32_t kCols = kN <= 64 ? 64 : (kN <= 128 ? 128 : (kN <= 256 ? 256 : 512));
+  constexpr uint32_t kIdesc = InstrDescS8(kNMma);
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_w[kMaxStages], full_x[kMaxStages], empty[kMaxStages], cfull[kConvBufs],
-      cempty[kConvBufs], accf;
+  __shared__ __align__(8) uint64_t full_w[S], full_x[S], empty[S], xready, accf;
   __shared__ uint32_t tmem_s;
+  __shared__ int32_t exp_s[R];
+  __shared__ uint32_t amax_s[M == kAPlanes ? 1 : 2 * R];
   __shared__ double inv_s[M == kANorm ? R : 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t raw_addr = SmemAddr(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
-  uint8_t* conv_base = smem + L::kStageArea;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kBn;
   const int64_t row0 = static_cast<int64_t>(blockIdx.z) * R;
   const int kb_begin = blockIdx.y * g.kb_per_split;
@@ -324,12 +363,9 @@ __global__ void __launch_bounds__(kThreads, (R == 16 && M == kAPlanes) ? 3 : 1)
     for (int s = 0; s < S; ++s) {
       MbarInit(&full_w[s], 1);
       MbarInit(&full_x[s], 1);
-      MbarInit(&empty[s], 1 + kConvWarps);
+      MbarInit(&empty[s], 1);
     }
-    for (int c = 0; c < kConvBufs; ++c) {
-      MbarInit(&cfull[c], kConvWarps);
-      MbarInit(&cempty[c], 1);
-    }
+    MbarInit(&xready, kConvWarps);
     MbarInit(&accf, 1);
     FenceBarrierInit();
   }
@@ -346,123 +382,100 @@ __global__ void __launch_bounds__(kThreads, (R == 16 && M == kAPlanes) ? 3 : 1)
       // Weights of the first stages before the wait: they are immutable.
       const int pre = min(S, nkb);
       for (int i = 0; i < pre; ++i) {
-        MbarArriveExpectTx(&full_w[i], kWRaw);
+        MbarArriveExpectTx(&full_w[i], kWBytes);
         TmaLoad2D(smem + i * L::kStage + L::kXBytes, &tw, static_cast<int32_t>(n0), (kb_begin + i) * kBk, &full_w[i]);
       }
-      PdlWait();
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S;
-        uint8_t* stage = smem + s * L::kStage;
-        const int32_t k0 = (kb_begin + i) * kBk;
-        if (i >= S) {
-          ok &= MbarWait(&empty[s], ((i / S) & 1) ^ 1);
-          MbarArriveExpectTx(&full_w[s], kWRaw);
-          TmaLoad2D(stage + L::kXBytes, &tw, static_cast<int32_t>(n0), k0, &full_w[s]);
-        }
-        MbarArriveExpectTx(&full_x[s], L::kXLoad);
-        if constexpr (M == kAPlanes) {
+      if constexpr (M == kAPlanes) {
+        PdlWait();
+        for (int i = 0; i < nkb; ++i) {
+          const int s = i % S;
+          uint8_t* stage = smem + s * L::kStage;
+          const int32_t k0 = (kb_begin + i) * kBk;
+          if (i >= S) {
+            ok &= MbarWait(&empty[s], ((i / S) & 1) ^ 1);
+            MbarArriveExpectTx(&full_w[s], kWBytes);
+            TmaLoad2D(stage + L::kXBytes, &tw, static_cast<int32_t>(n0), k0, &full_w[s]);
+          }
+          MbarArriveExpectTx(&full_x[s], L::kXBytes);
           TmaLoad3D(stage, &tx, k0, static_cast<int32_t>(row0), 0, &full_x[s]);
-        } else {
-          uint8_t* xraw = stage + L::kXBytes + kWRaw;
-          TmaLoad2D(xraw, &tx, k0, static_cast<int32_t>(row0), &full_x[s]);
-          if constexpr (M == kASilu) TmaLoad2D(xraw + R * 256, &tu, k0, static_cast<int32_t>(row0), &full_x[s]);
+        }
+      } else {
+        // The fp32 tiles of every k block of the CTA, one barrier per block.
+        PdlWait();
+        float* ytiles = reinterpret_cast<float*>(smem + S * L::kStage);
+        for (int i = 0; i < nkb; ++i) {
+          const int32_t k0 = (kb_begin + i) * kBk;
+          float* dst = ytiles + i * L::kYTiles * R * kBk;
+          MbarArriveExpectTx(&full_x[i], L::kYTiles * L::kYTile);
+          TmaLoad2D(dst, &tx, k0, static_cast<int32_t>(row0), &full_x[i]);
+          if constexpr (M == kASilu) TmaLoad2D(dst + R * kBk, &tu, k0, static_cast<int32_t>(row0), &full_x[i]);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Nothing for the MMA arrives before the previous kernel completes: wait
+      // in griddepcontrol.wait (no issue slots) rather than polling barriers
+      // while that kernel still runs on this SM.
+      PdlWait();
+      if constexpr (M != kAPlanes) ok &= MbarWait(&xready, 0);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % S, c = i % kConvBufs;
+        const int s = i % S;
+        ok &= MbarWait(&full_w[s], (i / S) & 1);
         if constexpr (M == kAPlanes) ok &= MbarWait(&full_x[s], (i / S) & 1);
-        ok &= MbarWait(&cfull[c], (i / kConvBufs) & 1);
         TcFenceAfterSync();
-        const uint32_t a_addr = SmemAddr(conv_base + c * kWConv);
         const uint32_t b_addr = SmemAddr(smem + s * L::kStage);
+        const uint32_t a_addr = b_addr + L::kXBytes;
 #pragma unroll
         for (int ks = 0; ks < kBk / kMmaK; ++ks) {
-          // A (weights, n-contiguous): 16 k = two k atoms = 4096 bytes per step;
-          // n atoms 1024 apart (LBO), k atoms 2048 apart (SBO). B (planes,
-          // k-contiguous): 32 bytes of k per step inside the swizzled row;
-          // 8-row groups 1024 apart (SBO); planes R * 128 bytes apart.
-          const uint64_t adesc = SmemDescSw128(a_addr + ks * 4096, 1024, 2048);
-          if constexpr (kOneMma) {
-            MmaBf16(tmem, adesc, SmemDescSw128(b_addr + ks * 32, 16, 1024), kIdesc, (i | ks) != 0);
-          } else {
+          // A (weights, n-contiguous; the 128 features are one 128-byte atom,
+          // so there is no second atom for LBO to locate): 32 k rows = 4096
+          // bytes per step, 8-row k groups 1024 apart (SBO).
+          // B (digit rows, k-contiguous): 32 bytes of k per step inside the
+          // swizzled row; 8-row groups 1024 apart (SBO).
+          const uint64_t adesc = SmemDescSw128(a_addr + ks * (kMmaK * kBn), 0, 1024);
 #pragma unroll
-            for (int p = 0; p < 3; ++p) {
-              const uint64_t bdesc = SmemDescSw128(b_addr + p * R * 128 + ks * 32, 16, 1024);
-              MmaBf16(tmem + p * R, adesc, bdesc, kIdesc, (i | ks) != 0);
-            }
+          for (int mm = 0; mm < kMmas; ++mm) {
+            const uint64_t bdesc = SmemDescSw128(b_addr + mm * kNMma * kBk + ks * kMmaK, 16, 1024);
+            MmaS8(tmem + mm * kNMma, adesc, bdesc, kIdesc, (i | ks) != 0);
           }
         }
         MmaCommit(&empty[s]);
-        MmaCommit(&cempty[c]);
       }
       if (nkb > 0) MmaCommit(&accf);
     }
   } else {
     const int ct = tid - 64;
     const int valid = static_cast<int>(Min64(R, g.m - row0));
-    if constexpr (M != kAPlanes) {
-      // Rows past the matrix: zero planes in every stage, written once.
-      if (valid < R) {
-        for (int s = 0; s < S; ++s) {
-          uint8_t* planes = smem + s * L::kStage;
-          for (int idx = ct; idx < 3 * (R - valid) * 8; idx += kConvWarps * 32) {
-            const int p = idx / ((R - valid) * 8), rem = idx % ((R - valid) * 8);
-            *reinterpret_cast<uint4*>(planes + p * R * 128 + (valid + rem / 8) * 128 + (rem % 8) * 16) =
-                make_uint4(0, 0, 0, 0);
+    PdlWait();
+    if constexpr (M == kAPlanes) {
+      if (ct < R) exp_s[ct] = ct < valid ? g.row_exp[blockIdx.y * g.m + row0 + ct] : 0;
+      if (nkb > 0) ok &= MbarWaitSleep(&accf, 0);
+    } else {
+      if constexpr (M == kANorm) {
+        // Row RMS of the valid rows: from the producer's sums of squares when
+        // given, else from the whole rows of A.
+        if (g.sq_in != nullptr) {
+          if (ct < valid) {
+            const double* p = g.sq_in + (row0 + ct) * g.sq_ld;
+            double sum = 0.0;
+            for (int t = 0; t < g.sq_n; ++t) sum += p[t];
+            inv_s[ct] = 1.0 / sqrt(sum / static_cast<double>(g.k) + static_cast<double>(g.eps));
           }
+        } else {
+          TileInverseRms<R, kConvWarps>(g.a, g.lda, row0, valid, g.k, g.eps, ct, inv_s);
         }
+        if (ct >= valid && ct < R) inv_s[ct] = 0.0;  // rows past the matrix (their tiles read as zero)
+        asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
       }
-    }
-    // The first weight blocks (one per conversion buffer) are converted before
-    // anything waits for the activations: the weights are immutable, so this
-    // overlaps the previous kernel, and after the activations land only the
-    // split stands between them and the MMA.
-    const int pre = min(kConvBufs, nkb);
-    for (int i = 0; i < pre; ++i) {
-      ok &= MbarWait(&full_w[i % S], (i / S) & 1);
-      ConvertWeightBlock(smem + (i % S) * L::kStage + L::kXBytes, conv_base + i * kWConv, ct);
-    }
-    if constexpr (M == kANorm) {
-      // Row RMS of the valid rows: from the producer's sums of squares when
-      // given, else from the whole rows of A.
-      PdlWait();
-      if (g.sq_in != nullptr) {
-        if (ct < valid) {
-          const double* p = g.sq_in + (row0 + ct) * g.sq_ld;
-          double sum = 0.0;
-          for (int t = 0; t < g.sq_n; ++t) sum += p[t];
-          inv_s[ct] = 1.0 / sqrt(sum / static_cast<double>(g.k) + static_cast<double>(g.eps));
-        }
-      } else {
-        TileInverseRms<R>(g.a, g.lda, row0, valid, g.k, g.eps, ct, inv_s);
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
-    }
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % S, c = i % kConvBufs;
-      uint8_t* stage = smem + s * L::kStage;
-      if (i >= pre) {
-        ok &= MbarWait(&full_w[s], (i / S) & 1);
-        ok &= MbarWait(&cempty[c], ((i / kConvBufs) & 1) ^ 1);
-        ConvertWeightBlock(stage + L::kXBytes, conv_base + c * kWConv, ct);
-      }
-      if constexpr (M != kAPlanes) {
-        ok &= MbarWait(&full_x[s], (i / S) & 1);
-        const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBk;
-        SplitTile<R, M>(stage + L::kXBytes + kWRaw, stage, ct, valid, M == kANorm ? g.gamma + k0 : nullptr,
-                        static_cast<int>(Min64(kBk, g.k - k0)), inv_s);
-      }
+      for (int i = 0; i < nkb; ++i) ok &= MbarWait(&full_x[i], 0);
+      BuildDigits<R, M, kConvWarps>(g, nkb, static_cast<int64_t>(kb_begin) * kBk, inv_s,
+                        reinterpret_cast<float*>(smem + S * L::kStage), amax_s, exp_s, smem, L::kStage, ct);
       FenceProxyAsyncSmem();
       __syncwarp();
-      if (lane == 0) {
-        MbarArrive(&cfull[c]);
-        MbarArrive(&empty[s]);
-      }
+      if (lane == 0) MbarArrive(&xready);
+      if (nkb > 0) ok &= MbarWait(&accf, 0);
     }
-    if (nkb > 0) ok &= MbarWait(&accf, 0);
   }
   // Every thread past this point may read the residual or write the output.
   PdlWait();
@@ -482,24 +495,45 @@ __global__ void __launch_bounds__(kThreads, (R == 16 && M == kAPlanes) ? 3 : 1)
   const int splits = static_cast<int>(gridDim.y);
   const int64_t rows = Min64(R, g.m - row0);
   const int64_t cols = Min64(kBn, g.n - n0);
-  float* tile = reinterpret_cast<float*>(smem);  // [R][128] fp32; the stage memory is idle now
+  float* tile = reinterpret_cast<float*>(smem);  // [R][kBn], over the stages
   if (warp >= 2) {
-    const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. +31
+    // Thread (quarter, lane) holds feature 32 * quarter + lane: its TMEM lane.
+    // Column p * R + r holds digit plane p of row r. With eight converter
+    // warps, the two warps of a quarter take alternate 16-row chunks.
+    const int quarter = warp & 3;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    constexpr int kChunk = R < 32 ? R : 32;  // TMEM columns per load
+    constexpr int kChunk = 16;
+    constexpr int kWarpsPerQuarter = kConvWarps / 4;
 #pragma unroll 1
-    for (int c0 = 0; c0 < R; c0 += kChunk) {
+    for (int c0 = ((warp - 2) >> 2) * kChunk; c0 < R; c0 += kChunk * kWarpsPerQuarter) {
       float v[kChunk];
       if (nkb > 0 && cta_ok) {
-        // hi + mid + lo, each accumulated separately over K.
-        float w[kChunk];
-        TmemLoadCols(lane_base + c0, v);
-        TmemLoadCols(lane_base + R + c0, w);
+        uint32_t d[kDigits][kChunk];
 #pragma unroll
-        for (int j = 0; j < kChunk; ++j) v[j] += w[j];
-        TmemLoadCols(lane_base + 2 * R + c0, w);
+        for (int p = 0; p < kDigits; ++p) TmemLoad16Raw(lane_base + p * R + c0, d[p]);
+        TmemWaitLoads();
 #pragma unroll
-        for (int j = 0; j < kChunk; ++j) v[j] += w[j];
+        for (int j = 0; j < kChunk; ++j) {
+          const int32_t e = exp_s[c0 + j];
+          // The exact sum of the planes, rounded once; then the exact scaling
+          // by 2^(e - 30) (a normal float for every exponent a row takes).
+          // In-kernel operands walk at most 256 k, so every partial sum is an
+          // integer below 2^46 and the double arithmetic is exact.
+          float t;
+          if constexpr (M != kAPlanes) {
+            const double s = fma(static_cast<double>(static_cast<int32_t>(d[0][j])), 16777216.0,
+                                 fma(static_cast<double>(static_cast<int32_t>(d[1][j])), 65536.0,
+                                     fma(static_cast<double>(static_cast<int32_t>(d[2][j])), 256.0,
+                                         static_cast<double>(static_cast<int32_t>(d[3][j])))));
+            t = __double2float_rn(s);
+          } else {
+            t = __ll2float_rn((static_cast<long long>(static_cast<int32_t>(d[0][j])) << 24) +
+                              (static_cast<long long>(static_cast<int32_t>(d[1][j])) << 16) +
+                              (static_cast<long long>(static_cast<int32_t>(d[2][j])) << 8) +
+                              static_cast<long long>(static_cast<int32_t>(d[3][j])));
+          }
+          v[j] = e == kBadRow ? __int_as_float(0x7fc00000) : __fmul_rn(t, __int_as_float((127 - 30 + e) << 23));
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) v[j] = cta_ok ? 0.f : __int_as_float(0x7fc00000);
@@ -645,86 +679,99 @@ __global__ void __launch_bounds__(kThreads, (R == 16 && M == kAPlanes) ? 3 : 1)
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // peers are done with this tile
 }
 
-// fp32 [m, k] (row stride lda) -> three bf16 planes [3][m][k] (Split3). With
-// `up` set, the element is SiluMul(a[r][i], up[r][i]) first.
-__global__ void SplitPlanesKernel(const float* __restrict__ a, const float* __restrict__ up, int64_t lda, int64_t m,
-                                  int64_t k, __nv_bfloat16* __restrict__ planes) {
-  PdlTrigger();
-  PdlWait();
-  const int64_t quads = k / 4;
-  const int64_t total = m * quads;
-  const int64_t plane = m * k;
-  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = idx / quads, q = idx - r * quads;
-    const float4 v = __ldg(reinterpret_cast<const float4*>(a + r * lda + q * 4));
-    float x[4] = {v.x, v.y, v.z, v.w};
-    if (up != nullptr) {
-      const float4 u = __ldg(reinterpret_cast<const float4*>(up + r * lda + q * 4));
-      x[0] = SiluMul(x[0], u.x);
-      x[1] = SiluMul(x[1], u.y);
-      x[2] = SiluMul(x[2], u.z);
-      x[3] = SiluMul(x[3], u.w);
-    }
-    float hi[4], mid[4], lo[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) Split3(x[i], &hi[i], &mid[i], &lo[i]);
-    const int64_t off = r * k + q * 4;
-    *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(hi[0], hi[1]), PackBf16(hi[2], hi[3]));
-    *reinterpret_cast<uint2*>(planes + plane + off) = make_uint2(PackBf16(mid[0], mid[1]), PackBf16(mid[2], mid[3]));
-    *reinterpret_cast<uint2*>(planes + 2 * plane + off) = make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
-  }
-}
+// Planes mode operand. Segment s of row r (k in [s * seg, min(k, (s + 1) *
+// seg)): the range CTA s of a split-K cluster walks) is formed as the mode does
+// (M: kAF32, kASilu or kANorm), its exponent found over the segment, and its
+// four digit planes written (plane p of row r at p * m * kp + r * kp) with the
+// exponent at row_exp[s * m + r]. A group of 2^group_log2 threads (32 .. 256)
+// takes one (row, segment) item and keeps up to kDigitQuads quads per thread in
+// registers; a longer segment is formed twice.
+constexpr int kDigitQuads = 8;
+constexpr int kDigitThreads = 256;
 
-// RmsNorm rows then split: one warp per row computes the row's inverse RMS as
-// RmsNormKernel does and writes the three planes of float(double(x) * inv) * w.
-__global__ void SplitPlanesNormKernel(const float* __restrict__ a, int64_t lda, const float* __restrict__ gamma,
-                                      float eps, int64_t m, int64_t k, __nv_bfloat16* __restrict__ planes) {
+template <int M>
+__global__ void __launch_bounds__(kDigitThreads)
+    DigitPlanesKernel(const float* __restrict__ a, const float* __restrict__ up, int64_t lda,
+                      const float* __restrict__ gamma, float eps, int64_t m, int64_t k, int64_t kp, int64_t seg,
+                      int64_t nseg, uint8_t* __restrict__ planes, int32_t* __restrict__ row_exp, int group_log2) {
+  __shared__ uint32_t part[kDigitThreads / 32];
+  __shared__ double inv_sh[kDigitThreads / 32];
   PdlTrigger();
   PdlWait();
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  const int64_t plane = m * k;
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < m; r += warps) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int group_threads = 1 << group_log2, groups = kDigitThreads >> group_log2;
+  const int gi = tid >> group_log2, t = tid & (group_threads - 1);
+  const int64_t items = m * nseg, plane = m * kp;
+  // The loop bound is the same for every thread of the CTA (barriers inside).
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * groups; base < items;
+       base += static_cast<int64_t>(gridDim.x) * groups) {
+    const int64_t item = base + gi;
+    const bool live = item < items;
+    const int64_t r = live ? item / nseg : 0, sg = live ? item % nseg : 0;
+    const int64_t k0 = sg * seg;
+    const int64_t quads = live ? Min64(seg, k - k0) / 4 : 0;
     const float* in = a + r * lda;
-    const double iv = RowInverseRms(in, k, eps, lane);
-    for (int64_t q = lane; q < k / 4; q += 32) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(in + q * 4));
-      const float4 w = __ldg(reinterpret_cast<const float4*>(gamma + q * 4));
-      const float x[4] = {__fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), w.x),
-                          __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), w.y),
-                          __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), w.z),
-                          __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), w.w)};
-      float hi[4], mid[4], lo[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) Split3(x[i], &hi[i], &mid[i], &lo[i]);
-      const int64_t off = r * k + q * 4;
-      *reinterpret_cast<uint2*>(planes + off) = make_uint2(PackBf16(hi[0], hi[1]), PackBf16(hi[2], hi[3]));
-      *reinterpret_cast<uint2*>(planes + plane + off) =
-          make_uint2(PackBf16(mid[0], mid[1]), PackBf16(mid[2], mid[3]));
-      *reinterpret_cast<uint2*>(planes + 2 * plane + off) =
-          make_uint2(PackBf16(lo[0], lo[1]), PackBf16(lo[2], lo[3]));
+    const float* uin = M == kASilu ? up + r * lda + k0 : nullptr;
+    const float* gam = M == kANorm ? gamma + k0 : nullptr;
+    double inv = 0.0;
+    if constexpr (M == kANorm) {
+      if (t < 32 && live) {
+        const double iv = RowInverseRms(in, k, eps, lane);  // the whole row, as RmsNormKernel sums it
+        if (lane == 0) inv_sh[gi] = iv;
+      }
+      __syncthreads();
+      inv = inv_sh[gi];
     }
+    float4 y[kDigitQuads];
+    uint32_t amax = 0;
+#pragma unroll
+    for (int j = 0; j < kDigitQuads; ++j) {
+      const int64_t q = t + static_cast<int64_t>(j) * group_threads;
+      y[j] = q < quads ? FormQuad<M>(in + k0, uin, gam, inv, q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      amax = max(amax, AbsMaxBits(y[j]));
+    }
+    for (int64_t q = t + static_cast<int64_t>(kDigitQuads) * group_threads; q < quads; q += group_threads) {
+      amax = max(amax, AbsMaxBits(FormQuad<M>(in + k0, uin, gam, inv, q)));
+    }
+    amax = __reduce_max_sync(kFull, amax);
+    if (lane == 0) part[warp] = amax;
+    __syncthreads();
+    uint32_t gmax = 0;
+    for (int w = gi * (group_threads >> 5); w < (gi + 1) * (group_threads >> 5); ++w) gmax = max(gmax, part[w]);
+    const int32_t e = RowExponent(gmax);
+    __syncthreads();  // `part` is rewritten by the next item
+    uint8_t* dst = planes + r * kp + k0;
+#pragma unroll
+    for (int j = 0; j < kDigitQuads; ++j) {
+      const int64_t q = t + static_cast<int64_t>(j) * group_threads;
+      if (q < quads) {
+        uint32_t w[kDigits] = {0u, 0u, 0u, 0u};
+        if (e != kBadRow) FourDigits(y[j], FixScale(e), w);
+#pragma unroll
+        for (int p = 0; p < kDigits; ++p) *reinterpret_cast<uint32_t*>(dst + p * plane + 4 * q) = w[p];
+      }
+    }
+    for (int64_t q = t + static_cast<int64_t>(kDigitQuads) * group_threads; q < quads; q += group_threads) {
+      uint32_t w[kDigits] = {0u, 0u, 0u, 0u};
+      if (e != kBadRow) FourDigits(FormQuad<M>(in + k0, uin, gam, inv, q), FixScale(e), w);
+#pragma unroll
+      for (int p = 0; p < kDigits; ++p) *reinterpret_cast<uint32_t*>(dst + p * plane + 4 * q) = w[p];
+    }
+    if (live && t == 0) row_exp[sg * m + r] = e;
   }
 }
 
 struct TcPlan {
   int r;
   int mode;  // AMode
-  int stages;
   int64_t feature_tiles, row_tiles;
   int32_t kb_total, kb_per_split, splits;
-  size_t planes_bytes;
+  int64_t kp;           // digit plane row stride (bytes)
+  size_t digits_bytes;  // planes mode: the digit planes in the workspace (1024-aligned)
+  size_t planes_bytes;  // planes mode: digit planes and segment exponents
 };
 
-// Stages that fit the shared memory of one CTA (at most 4).
-template <int R, int M>
-constexpr int MaxStages() {
-  constexpr int stage = 3 * R * kBk * 2 + kWRaw + (M == kAPlanes ? 0 : (M == kASilu ? 2 : 1) * R * kBk * 4);
-  return stage * 4 + kConvBufs * kWConv + 1024 <= 227 * 1024 ? 4 : 3;
-}
-
-// Activation rows per tile (the MMA's N is three times this).
+// Activation rows per tile (the MMA's N is four times this).
 int64_t TileRows(int64_t m) { return m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128)); }
 
 TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
@@ -734,24 +781,26 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   p.row_tiles = CeilDiv(m, p.r);
   p.kb_total = static_cast<int32_t>(CeilDiv(k, kBk));
   // When the tile grid is smaller than the GPU, split K across a cluster of up
-  // to 8 CTAs, aiming at about two CTAs per SM and at least two k blocks per
-  // CTA (a CTA's hand-offs per k block, not bandwidth, bound small products).
+  // to 8 CTAs: the largest split whose grid still fits in one wave of the CTAs
+  // an SM holds (three at R = 16, two at R = 32, one above).
   const int64_t base = p.feature_tiles * p.row_tiles;
   int64_t splits = 1;
   if (base < kSms && p.kb_total > 1) {
-    // R = 16 tiles run three CTAs per SM: the largest split whose grid fits
-    // in one wave of them.
-    splits = Min64(CeilDiv(p.kb_total, 2), p.r == 16 ? (3 * kSms) / base : CeilDiv(2 * kSms, base));
+    const int64_t per_sm = p.r == 16 ? 3 : (p.r == 32 ? 2 : 1);
+    splits = Min64(p.kb_total, Max64(1, per_sm * kSms / base));
     if (splits > 8) splits = 8;
   }
+  splits = Max64(splits, CeilDiv(p.kb_total, kMaxBlocksPerCta));  // TcEligible keeps this <= 8
   p.kb_per_split = static_cast<int32_t>(CeilDiv(p.kb_total, splits));
   p.splits = static_cast<int32_t>(CeilDiv(p.kb_total, p.kb_per_split));
-  p.stages = p.kb_per_split <= 2 ? 2 : 4;  // 4: as many as fit (MaxStages, or fewer for more CTAs per SM)
-  // Splitting fp32 tiles in the kernel saves the planes pass (one launch) but
-  // adds converter work to every k block: worth it for CTAs that walk few
+  // A CTA that forms its own operand saves the planes pass (one launch) but
+  // holds its whole k range in shared memory: worth it for CTAs that walk few
   // blocks (latency-bound decode products), not for long weight streams.
-  p.mode = p.r == 128 || p.kb_per_split > 4 ? kAPlanes : (silu ? kASilu : (norm ? kANorm : kAF32));
-  p.planes_bytes = p.mode == kAPlanes ? (static_cast<size_t>(3) * m * k * 2 + 1023) / 1024 * 1024 : 0;
+  const bool planes = p.r == 128 || p.kb_per_split > kInKernelBlocks;
+  p.mode = planes ? kAPlanes : (silu ? kASilu : (norm ? kANorm : kAF32));
+  p.kp = (k + 15) / 16 * 16;
+  p.digits_bytes = planes ? (static_cast<size_t>(kDigits) * m * p.kp + 1023) / 1024 * 1024 : 0;
+  p.planes_bytes = planes ? p.digits_bytes + (static_cast<size_t>(p.splits) * m * 4 + 1023) / 1024 * 1024 : 0;
   return p;
 }
 
@@ -781,35 +830,30 @@ int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu
   });
   const dim3 grid(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
                   static_cast<unsigned>(p.row_tiles));
-  return CheckLaunchEx(LaunchK(Q8GemmTcKernel<R, ST, M>, grid, dim3(kThreads), L::kSmem, s, 1u,
+  return CheckLaunchEx(LaunchK(Q8GemmTcKernel<R, ST, M>, grid, dim3(Threads<M>()), L::kSmem, s, 1u,
                                static_cast<unsigned>(p.splits), tw, tx, tu, g),
                        "matmul_q8_tc");
 }
 
-template <int R, int M>
-int LaunchTcStages(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
-                   const TcPlan& p, cudaStream_t s) {
-  if (p.stages == 2) return LaunchTc<R, 2, M>(tw, tx, tu, g, p, s);
-  // Long weight streams with few rows (planes mode): fewer stages leave room
-  // for more CTAs per SM, and so more converter warps per SM: two at R = 32
-  // with three stages, three at R = 16 with two.
-  if constexpr (R == 16 && M == kAPlanes) {
-    return LaunchTc<R, 2, M>(tw, tx, tu, g, p, s);
-  } else if constexpr (R == 32 && M == kAPlanes) {
-    return LaunchTc<R, 3, M>(tw, tx, tu, g, p, s);
-  } else {
-    return LaunchTc<R, MaxStages<R, M>(), M>(tw, tx, tu, g, p, s);
-  }
-}
-
-// In-kernel split modes run at R <= 64 (the plan takes planes at R = 128).
+// In-kernel operand modes run at R <= 64 (the plan takes planes at R = 128).
 template <int M>
 int LaunchTcRows(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
                  const TcPlan& p, cudaStream_t s) {
   switch (p.r) {
-    case 16: return LaunchTcStages<16, M>(tw, tx, tu, g, p, s);
-    case 32: return LaunchTcStages<32, M>(tw, tx, tu, g, p, s);
-    default: return LaunchTcStages<64, M>(tw, tx, tu, g, p, s);
+    case 16: return LaunchTc<16, kInKernelBlocks, M>(tw, tx, tu, g, p, s);
+    case 32: return LaunchTc<32, kInKernelBlocks, M>(tw, tx, tu, g, p, s);
+    default: return LaunchTc<64, kInKernelBlocks, M>(tw, tx, tu, g, p, s);
+  }
+}
+
+// Planes mode, stages by tile rows: as many CTAs per SM as fit (three at R =
+// 16, two at R = 32, one above) with the stages that leaves room for.
+int LaunchTcPlanes(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
+  switch (p.r) {
+    case 16: return LaunchTc<16, 3, kAPlanes>(tw, tx, tx, g, p, s);
+    case 32: return LaunchTc<32, 3, kAPlanes>(tw, tx, tx, g, p, s);
+    case 64: return LaunchTc<64, 4, kAPlanes>(tw, tx, tx, g, p, s);
+    default: return LaunchTc<128, 2, kAPlanes>(tw, tx, tx, g, p, s);
   }
 }
 
@@ -826,14 +870,17 @@ bool Encode2D(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint
 }  // namespace
 
 // Whether the tensor-core path takes this product: a per-column or single
-// scale without zero points; weight rows a multiple of 16 bytes and
-// activation rows a multiple of 8 elements (TMA strides); 16-byte aligned.
+// scale without zero points; weight rows a multiple of 16 bytes (TMA stride)
+// and activation rows a multiple of 8 elements; 16-byte aligned; at most 8 x
+// 2^17 k (the int32 sums of a CTA hold 2^17 k).
 bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
                 int64_t n) {
   if (zero != nullptr || (axis != 1 && axis != -1)) return false;
   if (m <= 0 || k <= 0 || n <= 0 || n % 16 != 0 || k % 8 != 0 || lda % 4 != 0) return false;
   if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || reinterpret_cast<uintptr_t>(w) % 16 != 0) return false;
-  if (k > (int64_t{1} << 31) - 1 || n > (int64_t{1} << 31) - 1 || m > (int64_t{1} << 31) - 1) return false;
+  if (k > int64_t{8} * kMaxBlocksPerCta * kBk || n > (int64_t{1} << 31) - 1 || m > (int64_t{1} << 31) - 1) {
+    return false;
+  }
   return CeilDiv(m, TileRows(m)) <= 65535 && EncodeFn() != nullptr;
 }
 
@@ -855,34 +902,51 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
   }
   CUtensorMap tw{}, tx{}, tu{};
-  if (!Encode2D(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, n, k, n, kBn, kBk, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+  // Weight blocks [128 k][128 n] with 128-byte swizzle: the MMA's MN-major layout.
+  if (!Encode2D(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, n, k, n, kBn, kBk, CU_TENSOR_MAP_SWIZZLE_128B)) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: weight tensor map rejected");
   }
+  const int32_t* row_exp = nullptr;
   if (p.mode == kAPlanes) {
-    auto* planes = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) + kCounterRegion);
-    const int64_t total = m * (k / 4);
-    const int64_t blocks = CeilDiv(total, 256);
-    const int grid = static_cast<int>(blocks < kSms * 16 ? blocks : kSms * 16);
-    const int rc =
-        gamma != nullptr
-            ? CheckLaunchEx(LaunchK(SplitPlanesNormKernel, dim3(static_cast<unsigned>(Min64(CeilDiv(m, 8), kSms * 16))),
-                                    dim3(256), 0, stream, 1u, 1u, a, lda, gamma, eps, m, k, planes),
-                            "matmul_q8_split_norm")
-            : CheckLaunchEx(LaunchK(SplitPlanesKernel, dim3(grid), dim3(256), 0, stream, 1u, 1u, a, up, lda, m, k,
-                                    planes),
-                            "matmul_q8_split");
+    auto* planes = static_cast<uint8_t*>(workspace) + kCounterRegion;
+    auto* exps = reinterpret_cast<int32_t*>(planes + p.digits_bytes);
+    row_exp = exps;
+    // Threads per (row, segment): enough for kDigitQuads quads each.
+    const int64_t seg = static_cast<int64_t>(p.kb_per_split) * kBk;
+    const int64_t quads = Min64(seg, k) / 4;
+    int group_log2 = 5;
+    while (group_log2 < 8 && (int64_t{1} << group_log2) * kDigitQuads < quads) ++group_log2;
+    const int64_t items = m * p.splits;
+    const int64_t groups = kDigitThreads >> group_log2;
+    const dim3 grid(static_cast<unsigned>(Min64(CeilDiv(items, groups), kSms * 16)));
+    const int64_t nseg = p.splits;
+    const float* none = nullptr;
+    int rc;
+    if (gamma != nullptr) {
+      rc = CheckLaunchEx(LaunchK(DigitPlanesKernel<kANorm>, grid, dim3(kDigitThreads), 0, stream, 1u, 1u, a, none, lda,
+                                 gamma, eps, m, k, p.kp, seg, nseg, planes, exps, group_log2),
+                         "matmul_q8_digits_norm");
+    } else if (up != nullptr) {
+      rc = CheckLaunchEx(LaunchK(DigitPlanesKernel<kASilu>, grid, dim3(kDigitThreads), 0, stream, 1u, 1u, a, up, lda,
+                                 none, 0.f, m, k, p.kp, seg, nseg, planes, exps, group_log2),
+                         "matmul_q8_digits_silu");
+    } else {
+      rc = CheckLaunchEx(LaunchK(DigitPlanesKernel<kAF32>, grid, dim3(kDigitThreads), 0, stream, 1u, 1u, a, none, lda,
+                                 none, 0.f, m, k, p.kp, seg, nseg, planes, exps, group_log2),
+                         "matmul_q8_digits");
+    }
     if (rc != ACCEL_B200_OK) return rc;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m), 3};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(k) * 2, static_cast<cuuint64_t>(m) * k * 2};
-    const cuuint32_t box[3] = {kBk, static_cast<cuuint32_t>(p.r), 3};
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m), kDigits};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.kp), static_cast<cuuint64_t>(m) * p.kp};
+    const cuuint32_t box[3] = {kBk, static_cast<cuuint32_t>(p.r), kDigits};
     const cuuint32_t estr[3] = {1, 1, 1};
-    if (EncodeFn()(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, planes, dims, strides, box, estr,
+    if (EncodeFn()(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, planes, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
       return SetError(ACCEL_B200_EINVAL, "matmul_q8: activation tensor map rejected");
     }
   } else {
-    // fp32 tiles [R rows x 64 k]; rows and k beyond the matrix read as zero.
+    // fp32 tiles [R rows x 128 k]; rows and k beyond the matrix read as zero.
     const uint64_t row_bytes = static_cast<uint64_t>(lda) * 4;
     if (!Encode2D(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, k, m, row_bytes, kBk, p.r, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         (up != nullptr &&
@@ -893,12 +957,14 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   }
   TcArgs g{};
   g.a = a;
+  g.up = up;
   g.lda = lda;
   g.gamma = gamma;
   g.eps = eps;
   g.sq_in = sq_in;
   g.sq_ld = sq_ld;
   g.sq_n = sq_n;
+  g.row_exp = row_exp;
   g.m = m;
   g.k = k;
   g.n = n;
@@ -915,17 +981,12 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   for (int i = 0; i < g.peers.n; ++i) {
     if (reinterpret_cast<uintptr_t>(g.peers.c[i]) % 16 != 0) g.vec_store = 0;
   }
-  if (p.mode == kAPlanes) {
-    switch (p.r) {
-      case 16: return LaunchTcStages<16, kAPlanes>(tw, tx, tu, g, p, stream);
-      case 32: return LaunchTcStages<32, kAPlanes>(tw, tx, tu, g, p, stream);
-      case 64: return LaunchTcStages<64, kAPlanes>(tw, tx, tu, g, p, stream);
-      default: return LaunchTcStages<128, kAPlanes>(tw, tx, tu, g, p, stream);
-    }
+  switch (p.mode) {
+    case kAPlanes: return LaunchTcPlanes(tw, tx, g, p, stream);
+    case kASilu: return LaunchTcRows<kASilu>(tw, tx, tu, g, p, stream);
+    case kANorm: return LaunchTcRows<kANorm>(tw, tx, tu, g, p, stream);
+    default: return LaunchTcRows<kAF32>(tw, tx, tu, g, p, stream);
   }
-  if (p.mode == kASilu) return LaunchTcRows<kASilu>(tw, tx, tu, g, p, stream);
-  if (p.mode == kANorm) return LaunchTcRows<kANorm>(tw, tx, tu, g, p, stream);
-  return LaunchTcRows<kAF32>(tw, tx, tu, g, p, stream);
 }
 
 }  // namespace accel_b200

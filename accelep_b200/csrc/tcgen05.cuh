@@ -1,6 +1,7 @@
 // 5th-generation tensor core (tcgen05) helpers in inline PTX for sm_100a:
 // TMEM allocation, shared-memory matrix descriptors, the bf16 MMA with fp32
-// accumulation in TMEM, commit to an mbarrier, and TMEM loads.
+// accumulation and the int8 MMA with int32 accumulation in TMEM, commit to an
+// mbarrier, and TMEM loads.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -57,6 +58,29 @@ __host__ __device__ constexpr uint32_t InstrDescBf16(uint32_t n, bool a_mn_major
          | ((128u >> 4) << 24);               // M >> 4
 }
 
+// Instruction descriptor of kind::i8 with signed int8 A and B, int32 D,
+// M = 128; A stored M-contiguous (MN-major), B K-major. n: the MMA N (16..256, % 16).
+__host__ __device__ constexpr uint32_t InstrDescS8(uint32_t n) {
+  return (2u << 4)                 // D format: s32
+         | (1u << 7)               // A format: signed 8-bit
+         | (1u << 10)              // B format: signed 8-bit
+         | (1u << 15)              // A major: MN
+         | (0u << 16)              // B major: K
+         | ((n >> 3) << 17)        // N >> 3
+         | ((128u >> 4) << 24);    // M >> 4
+}
+
+// D[tmem] (+)= A[smem] x B[smem] in exact int32 arithmetic, issued by one thread.
+__device__ __forceinline__ void MmaS8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                      uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] x B[smem], issued by one thread.
 __device__ __forceinline__ void MmaBf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
@@ -109,5 +133,19 @@ __device__ __forceinline__ void TmemLoad16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane, raw, without
+// waiting: TmemWaitLoads() before the registers are read.
+__device__ __forceinline__ void TmemLoad16Raw(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void TmemWaitLoads() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 }  // namespace accel_b200

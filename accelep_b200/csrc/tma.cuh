@@ -81,4 +81,24 @@ __device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// The same wait with the suspending try_wait: the thread sleeps inside the
+// instruction until the phase completes or a hardware time limit passes. For
+// long waits of warps with nothing else to do, so that they take no issue
+// slots from the warps that work meanwhile.
+__device__ __forceinline__ bool MbarWaitSleep(uint64_t* bar, uint32_t parity) {
+  const long long start = clock64();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(SmemAddr(bar)), "r"(parity)
+        : "memory");
+    if (done != 0) return true;
+    if (clock64() - start > kWaitLimitCycles) return false;
+  }
+}
+
 }  // namespace accel_b200
