@@ -26,11 +26,11 @@
 // A row holding Inf or NaN yields NaN outputs.
 //
 // The MMA is issued "swapped": M = 128 runs over output features and N over
-// activation rows times digit planes (N = 4R; two MMAs of N = 256 at R = 128),
-// so decode with 32 rows is a full-width MMA.
+// activation rows times digit planes (N = 4R, at most 256), so decode with 32
+// rows is a full-width MMA.
 //
 // Activation operand, by mode:
-//   planes  (R = 128, or more than two k blocks per CTA): a separate pass
+//   planes  (m > 64, or more than two k blocks per CTA): a separate pass
 //           forms each row segment (plain, SiluMul or RmsNorm), finds its
 //           exponent and writes the digit planes [4][m][kp] and the exponents
 //           [segments][m] to the workspace; TMA loads [4][R][128 k] tiles with
@@ -89,12 +89,13 @@ constexpr int32_t kBadRow = 0x7fff;     // exponent of a row holding Inf or NaN
 constexpr int kMaxBlocksPerCta = 1024;  // 2^17 k: int32 sums of int8 x int8 cannot overflow
 constexpr int kInKernelBlocks = 2;      // k blocks of a CTA that forms its own operand
 // Converter warps: eight where they form the operand (latency-bound decode
-// products: more threads shorten the operand and epilogue work), four in
-// planes mode (long weight streams; R = 16 runs three CTAs per SM).
-template <int M>
-constexpr int ConvWarps() { return M == 0 ? 4 : 8; }
-template <int M>
-constexpr int Threads() { return (2 + ConvWarps<M>()) * 32; }
+// products: more threads shorten the operand and epilogue work) and where the
+// tile has 64 or more rows (the epilogue's work per thread); four for long
+// weight streams with few rows (R = 16 runs three CTAs per SM).
+template <int R, int M>
+constexpr int ConvWarps() { return (M == 0 && R < 64) ? 4 : 8; }
+template <int R, int M>
+constexpr int Threads() { return (2 + ConvWarps<R, M>()) * 32; }
 
 enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2, kANorm = 3 };
 
@@ -331,13 +332,13 @@ __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0
 
 // R = 16 planes kernels (long weight streams, m <= 16) run three CTAs per SM.
 template <int R, int kStagesT, int M>
-__global__ void __launch_bounds__(Threads<M>(), (R == 16 && M == kAPlanes) ? 3 : 1)
+__global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 3 : 1)
     Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                    const __grid_constant__ CUtensorMap tu, TcArgs g) {
   using L = Tc<R, kStagesT, M>;
   constexpr int S = L::kStages;
-  constexpr int kConvWarps = ConvWarps<M>();
-  constexpr int kThreads = Threads<M>();
+  constexpr int kConvWarps = ConvWarps<R, M>();
+  constexpr int kThreads = Threads<R, M>();
   constexpr int kN = kDigits * R;                 // MMA N over all digit planes
   constexpr int kMmas = kN <= 256 ? 1 : 2;        // R = 128: two MMAs of N = 256
   constexpr int kNMma = kN / kMmas;
@@ -515,23 +516,14 @@ __global__ void __launch_bounds__(Threads<M>(), (R == 16 && M == kAPlanes) ? 3 :
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
           const int32_t e = exp_s[c0 + j];
-          // The exact sum of the planes, rounded once; then the exact scaling
-          // by 2^(e - 30) (a normal float for every exponent a row takes).
-          // In-kernel operands walk at most 256 k, so every partial sum is an
-          // integer below 2^46 and the double arithmetic is exact.
-          float t;
-          if constexpr (M != kAPlanes) {
-            const double s = fma(static_cast<double>(static_cast<int32_t>(d[0][j])), 16777216.0,
-                                 fma(static_cast<double>(static_cast<int32_t>(d[1][j])), 65536.0,
-                                     fma(static_cast<double>(static_cast<int32_t>(d[2][j])), 256.0,
-                                         static_cast<double>(static_cast<int32_t>(d[3][j])))));
-            t = __double2float_rn(s);
-          } else {
-            t = __ll2float_rn((static_cast<long long>(static_cast<int32_t>(d[0][j])) << 24) +
-                              (static_cast<long long>(static_cast<int32_t>(d[1][j])) << 16) +
-                              (static_cast<long long>(static_cast<int32_t>(d[2][j])) << 8) +
-                              static_cast<long long>(static_cast<int32_t>(d[3][j])));
-          }
+          // The exact sum of the planes in int64 (wide multiply-adds), rounded
+          // once; then the exact scaling by 2^(e - 30) (a normal float for
+          // every exponent a row takes).
+          long long sum = static_cast<long long>(static_cast<int32_t>(d[3][j]));
+          sum += static_cast<long long>(static_cast<int32_t>(d[2][j])) * 256;
+          sum += static_cast<long long>(static_cast<int32_t>(d[1][j])) * 65536;
+          sum += static_cast<long long>(static_cast<int32_t>(d[0][j])) * 16777216;
+          const float t = __ll2float_rn(sum);
           v[j] = e == kBadRow ? __int_as_float(0x7fc00000) : __fmul_rn(t, __int_as_float((127 - 30 + e) << 23));
         }
       } else {
@@ -546,47 +538,66 @@ __global__ void __launch_bounds__(Threads<M>(), (R == 16 && M == kAPlanes) ? 3 :
   __syncthreads();
   if (warp == 1) TmemDealloc(tmem, kCols);
   if (splits == 1) {
-    // Thread t < 128 owns column t of the tile for every row.
-    if (cta_ok && tid < cols) {
-      const int64_t col = n0 + tid;
-      const float sc = g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + col);
-      if (g.peers.n == 0 && g.ep.row_sq == nullptr) {
-        // The common case, kept free of the optional outputs (a loop over peers
-        // inside this loop measured 30% slower on prefill-sized tiles).
-#pragma unroll 4
-        for (int64_t r = 0; r < rows; ++r) {
+    // Warp w takes rows w, w + warps, ...; lane l the columns 4l .. 4l + 3.
+    if (cta_ok) {
+      const int c4 = lane * 4;
+      float sc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
+      }
+      if (g.peers.n == 0 && g.ep.row_sq == nullptr && g.vec_store && cols == kBn) {
+        // The common case, kept free of the optional outputs.
+#pragma unroll 2
+        for (int r = warp; r < rows; r += kThreads / 32) {
           const int64_t row = row0 + r;
-          g.c[row * g.ldc + col] = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
+          const float4 v = *reinterpret_cast<const float4*>(tile + r * kBn + c4);
+          *reinterpret_cast<float4*>(g.c + row * g.ldc + n0 + c4) =
+              make_float4(ApplyEpilogue(g.ep, __fmul_rn(v.x, sc[0]), row, n0 + c4),
+                          ApplyEpilogue(g.ep, __fmul_rn(v.y, sc[1]), row, n0 + c4 + 1),
+                          ApplyEpilogue(g.ep, __fmul_rn(v.z, sc[2]), row, n0 + c4 + 2),
+                          ApplyEpilogue(g.ep, __fmul_rn(v.w, sc[3]), row, n0 + c4 + 3));
         }
       } else {
-        for (int64_t r = 0; r < rows; ++r) {
+        for (int r = warp; r < rows; r += kThreads / 32) {
           const int64_t row = row0 + r;
-          const float o = ApplyEpilogue(g.ep, __fmul_rn(tile[r * kBn + tid], sc), row, col);
-          g.c[row * g.ldc + col] = o;
-          StorePeers(g.peers, row * g.ldc + col, o);
-          if (g.ep.row_sq != nullptr) tile[r * kBn + tid] = o;
-        }
-      }
-    }
-    if (g.peers.n > 0) __threadfence_system();
-    if (g.ep.row_sq != nullptr) {
-      // Sums of squares of this tile's outputs per row: warp w of the first
-      // four takes rows w, w + 4, ...; lane l the columns 4l .. 4l + 3.
-      __syncthreads();
-      if (tid < 128 && cta_ok) {
-        for (int r = warp; r < rows; r += 4) {
           double sq = 0.0;
+          if (c4 < cols) {
+            const float4 v = *reinterpret_cast<const float4*>(tile + r * kBn + c4);
+            const float in[4] = {v.x, v.y, v.z, v.w};
+            float o[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (lane * 4 + q < cols) {
-              const double v = static_cast<double>(tile[r * kBn + lane * 4 + q]);
-              sq += v * v;
+            for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(in[q], sc[q]), row, n0 + c4 + q);
+            if (g.ep.row_sq != nullptr) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (c4 + q < cols) {
+                  const double dv = static_cast<double>(o[q]);
+                  sq += dv * dv;
+                }
+              }
+            }
+            const int64_t off = row * g.ldc + n0 + c4;
+            if (g.vec_store && c4 + 4 <= cols) {
+              *reinterpret_cast<float4*>(g.c + off) = make_float4(o[0], o[1], o[2], o[3]);
+              StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
+            } else {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                if (c4 + q < cols) {
+                  g.c[off + q] = o[q];
+                  StorePeers(g.peers, off + q, o[q]);
+                }
+              }
             }
           }
-          sq = WarpSum(sq);
-          if (lane == 0) g.ep.row_sq[(row0 + r) * g.ep.row_sq_ld + n0 / kBn] = sq;
+          if (g.ep.row_sq != nullptr) {  // the warp holds the row's columns of this tile
+            sq = WarpSum(sq);
+            if (lane == 0) g.ep.row_sq[row * g.ep.row_sq_ld + n0 / kBn] = sq;
+          }
         }
       }
+      if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes
     }
     return;
   }
@@ -771,8 +782,10 @@ struct TcPlan {
   size_t planes_bytes;  // planes mode: digit planes and segment exponents
 };
 
-// Activation rows per tile (the MMA's N is four times this).
-int64_t TileRows(int64_t m) { return m <= 16 ? 16 : (m <= 32 ? 32 : (m <= 64 ? 64 : 128)); }
+// Activation rows per tile (the MMA's N is four times this). Above 32 rows,
+// 64-row tiles: two CTAs (two stages each) share an SM, so that one CTA's
+// prologue and epilogue overlap the other's MMAs.
+int64_t TileRows(int64_t m) { return m <= 16 ? 16 : (m <= 32 ? 32 : 64); }
 
 TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   TcPlan p{};
@@ -782,11 +795,11 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   p.kb_total = static_cast<int32_t>(CeilDiv(k, kBk));
   // When the tile grid is smaller than the GPU, split K across a cluster of up
   // to 8 CTAs: the largest split whose grid still fits in one wave of the CTAs
-  // an SM holds (three at R = 16, two at R = 32, one above).
+  // an SM holds (three at R = 16, two above).
   const int64_t base = p.feature_tiles * p.row_tiles;
   int64_t splits = 1;
   if (base < kSms && p.kb_total > 1) {
-    const int64_t per_sm = p.r == 16 ? 3 : (p.r == 32 ? 2 : 1);
+    const int64_t per_sm = p.r == 16 ? 3 : 2;
     splits = Min64(p.kb_total, Max64(1, per_sm * kSms / base));
     if (splits > 8) splits = 8;
   }
@@ -796,7 +809,7 @@ TcPlan MakeTcPlan(int64_t m, int64_t k, int64_t n, bool silu, bool norm) {
   // A CTA that forms its own operand saves the planes pass (one launch) but
   // holds its whole k range in shared memory: worth it for CTAs that walk few
   // blocks (latency-bound decode products), not for long weight streams.
-  const bool planes = p.r == 128 || p.kb_per_split > kInKernelBlocks;
+  const bool planes = m > 64 || p.kb_per_split > kInKernelBlocks;
   p.mode = planes ? kAPlanes : (silu ? kASilu : (norm ? kANorm : kAF32));
   p.kp = (k + 15) / 16 * 16;
   p.digits_bytes = planes ? (static_cast<size_t>(kDigits) * m * p.kp + 1023) / 1024 * 1024 : 0;
@@ -830,12 +843,12 @@ int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu
   });
   const dim3 grid(static_cast<unsigned>(p.feature_tiles), static_cast<unsigned>(p.splits),
                   static_cast<unsigned>(p.row_tiles));
-  return CheckLaunchEx(LaunchK(Q8GemmTcKernel<R, ST, M>, grid, dim3(Threads<M>()), L::kSmem, s, 1u,
+  return CheckLaunchEx(LaunchK(Q8GemmTcKernel<R, ST, M>, grid, dim3(Threads<R, M>()), L::kSmem, s, 1u,
                                static_cast<unsigned>(p.splits), tw, tx, tu, g),
                        "matmul_q8_tc");
 }
 
-// In-kernel operand modes run at R <= 64 (the plan takes planes at R = 128).
+// In-kernel operand modes (m <= 64).
 template <int M>
 int LaunchTcRows(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
                  const TcPlan& p, cudaStream_t s) {
@@ -847,13 +860,12 @@ int LaunchTcRows(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap
 }
 
 // Planes mode, stages by tile rows: as many CTAs per SM as fit (three at R =
-// 16, two at R = 32, one above) with the stages that leaves room for.
+// 16, two at R = 32 and 64) with the stages that leaves room for.
 int LaunchTcPlanes(const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& g, const TcPlan& p, cudaStream_t s) {
   switch (p.r) {
     case 16: return LaunchTc<16, 3, kAPlanes>(tw, tx, tx, g, p, s);
     case 32: return LaunchTc<32, 3, kAPlanes>(tw, tx, tx, g, p, s);
-    case 64: return LaunchTc<64, 4, kAPlanes>(tw, tx, tx, g, p, s);
-    default: return LaunchTc<128, 2, kAPlanes>(tw, tx, tx, g, p, s);
+    default: return LaunchTc<64, 2, kAPlanes>(tw, tx, tx, g, p, s);
   }
 }
 
