@@ -33,6 +33,12 @@ class Epilogue(ctypes.Structure):
                 ("row_sq", c_vp), ("row_sq_ld", c_i64)]
 
 
+class L2Prefetch(ctypes.Structure):
+    """accel_b200_l2_prefetch (include/accel_b200.h)."""
+
+    _fields_ = [("ptr", c_vp * 4), ("bytes", c_i64 * 4), ("count", c_i32)]
+
+
 class LlamaConfig(ctypes.Structure):
     """AccelLlamaConfig (include/accel_b200_llama.h)."""
 
@@ -89,6 +95,9 @@ SIGNATURES = {
                                                     c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp]),
     "accel_b200_decode_attention": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
                                             c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]),
+    "accel_b200_decode_attention_prefetch": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp,
+                                                     c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp,
+                                                     ctypes.POINTER(L2Prefetch), c_vp]),
     "accel_b200_silu_mul_rows": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "accel_b200_sample_rows": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_f32, c_vp, c_i32, c_vp]),
     "accel_b200_greedy_step": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32,

@@ -65,7 +65,25 @@ struct FusedArgs {
   float* out;  // row r: heads * 64 at out + r * out_ld
   int64_t out_ld;
   int32_t* status;
+  accel_b200_l2_prefetch prefetch;  // ranges brought into L2 before the wait (count 0: none)
 };
+
+constexpr int64_t kPrefetchChunk = 32 * 1024;  // bytes per L2 prefetch instruction
+
+// This CTA's share of the prefetch ranges: chunk c of the ranges' 32 KiB
+// chunks goes to CTA c mod (CTAs).
+__device__ __forceinline__ void PrefetchShare(const accel_b200_l2_prefetch& pf) {
+  const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) * (blockIdx.y + static_cast<int64_t>(gridDim.y) *
+                                                                                       blockIdx.z);
+  const int64_t ctas = static_cast<int64_t>(gridDim.x) * gridDim.y * gridDim.z;
+  for (int i = 0; i < pf.count && i < 4; ++i) {
+    const char* base = static_cast<const char*>(pf.ptr[i]);
+    for (int64_t off = cta * kPrefetchChunk; off < pf.bytes[i]; off += ctas * kPrefetchChunk) {
+      const uint32_t n = static_cast<uint32_t>(Min64(kPrefetchChunk, pf.bytes[i] - off)) & ~15u;
+      if (n > 0) PrefetchL2(base + off, n);
+    }
+  }
+}
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a) {
@@ -77,6 +95,9 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   __shared__ __align__(16) float mo[G * kD];        // published weighted values
   __shared__ float m_run[G], l_run[G];
   PdlTrigger();
+  // Ranges for later kernels (immutable weights) go to L2 while this kernel
+  // waits for its inputs.
+  if (threadIdx.x == 0 && a.prefetch.count > 0) PrefetchShare(a.prefetch);
   PdlWait();  // row positions, q|k|v rows and the cache come from earlier kernels
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = static_cast<int>(blockIdx.x), S = static_cast<int>(gridDim.x);
@@ -114,10 +135,13 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
     float* kb = buf + (i & 1) * 2 * kChunkFloats;
     uint64_t* bar = &full[i & 1];
     if (copy > 0) {
+      // Read once per step: evict first, ahead of the weights the layer's
+      // products read next.
       const uint32_t bytes = static_cast<uint32_t>(copy) * kD * 4;
+      const uint64_t policy = EvictFirstPolicy();
       MbarArriveExpectTx(bar, 2 * bytes);
-      BulkCopyG2S(kb, kbase + t0 * kD, bytes, bar);
-      BulkCopyG2S(kb + kChunkFloats, vbase + t0 * kD, bytes, bar);
+      BulkCopyG2SHint(kb, kbase + t0 * kD, bytes, bar, policy);
+      BulkCopyG2SHint(kb + kChunkFloats, vbase + t0 * kD, bytes, bar, policy);
     } else {
       MbarArrive(bar);
     }
@@ -347,12 +371,11 @@ using namespace accel_b200;
 
 extern "C" {
 
-ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld, const int32_t* row_seq,
-                                               const int32_t* row_pos, int64_t rows, int32_t heads, int32_t kv_heads,
-                                               int32_t head_dim, const float* cos_table, const float* sin_table,
-                                               int32_t context, float* k_cache, float* v_cache, int64_t seq_stride,
-                                               int64_t head_stride, float* out, int64_t out_ld, int32_t* status,
-                                               void* stream) {
+ACCEL_B200_API int accel_b200_decode_attention_prefetch(
+    const float* qkv, int64_t qkv_ld, const int32_t* row_seq, const int32_t* row_pos, int64_t rows, int32_t heads,
+    int32_t kv_heads, int32_t head_dim, const float* cos_table, const float* sin_table, int32_t context,
+    float* k_cache, float* v_cache, int64_t seq_stride, int64_t head_stride, float* out, int64_t out_ld,
+    int32_t* status, const accel_b200_l2_prefetch* prefetch, void* stream) {
   if (rows < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim != kD || context <= 0 ||
       qkv == nullptr || row_pos == nullptr || cos_table == nullptr || sin_table == nullptr || k_cache == nullptr ||
       v_cache == nullptr || out == nullptr) {
@@ -372,9 +395,20 @@ ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld,
   }
   const int group = heads / kv_heads;
   if (group > kMaxG) return SetError(ACCEL_B200_EINVAL, "decode_attention: more than 8 query heads per kv head");
+  accel_b200_l2_prefetch pf{};
+  if (prefetch != nullptr) {
+    if (prefetch->count < 0 || prefetch->count > 4) return SetError(ACCEL_B200_EINVAL, "decode_attention: bad prefetch");
+    for (int i = 0; i < prefetch->count; ++i) {
+      if (prefetch->bytes[i] < 0 || (prefetch->bytes[i] > 0 && prefetch->ptr[i] == nullptr) ||
+          reinterpret_cast<uintptr_t>(prefetch->ptr[i]) % 16 != 0) {
+        return SetError(ACCEL_B200_EINVAL, "decode_attention: prefetch ranges must be 16-byte aligned");
+      }
+    }
+    pf = *prefetch;
+  }
   FusedArgs a{qkv,     qkv_ld,  row_seq,    row_pos,     cos_table, sin_table, k_cache,
               v_cache, seq_stride, head_stride, heads, kv_heads,  context,   1.f / sqrtf(static_cast<float>(kD)),
-              out,     out_ld,  status};
+              out,     out_ld,  status, pf};
   cudaStream_t s = AsStream(stream);
   switch (group) {
     case 1: return LaunchFused<1>(a, rows, s);
@@ -386,6 +420,17 @@ ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld,
     case 7: return LaunchFused<7>(a, rows, s);
     default: return LaunchFused<8>(a, rows, s);
   }
+}
+
+ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld, const int32_t* row_seq,
+                                               const int32_t* row_pos, int64_t rows, int32_t heads, int32_t kv_heads,
+                                               int32_t head_dim, const float* cos_table, const float* sin_table,
+                                               int32_t context, float* k_cache, float* v_cache, int64_t seq_stride,
+                                               int64_t head_stride, float* out, int64_t out_ld, int32_t* status,
+                                               void* stream) {
+  return accel_b200_decode_attention_prefetch(qkv, qkv_ld, row_seq, row_pos, rows, heads, kv_heads, head_dim,
+                                              cos_table, sin_table, context, k_cache, v_cache, seq_stride,
+                                              head_stride, out, out_ld, status, nullptr, stream);
 }
 
 }  // extern "C"

@@ -696,9 +696,22 @@ class Engine {
       NormGemm(hid, l.attn_norm, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr, normed, li > 0 ? sq : nullptr);
       if (decode && head_dim == 64) {
         // Rope, AppendCache and attention of the new rows in one kernel.
-        Abi(accel_b200_decode_attention(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
-                                        rope_cos.as<float>(), rope_sin.as<float>(), cfg.context, kc, vc, slot_stride,
-                                        head_stride, mixed.as<float>(), q_out, status.as<int32_t>(), stream));
+        // While it runs, the int8 weights of the products that follow (this
+        // layer's o, gate|up and down, then the next layer's q|k|v or, after
+        // the last layer, the LM head) go to L2.
+        accel_b200_l2_prefetch pf{};
+        const Group* next[4] = {&l.o, &l.gu, &l.down,
+                                li + 1 < cfg.layers ? &layers[static_cast<size_t>(li) + 1].qkv : &lm_head};
+        for (const Group* g : next) {
+          if (g == nullptr || g->kind != WKind::Q8) continue;
+          pf.ptr[pf.count] = g->w.p;
+          pf.bytes[pf.count] = g->k * g->n;
+          ++pf.count;
+        }
+        Abi(accel_b200_decode_attention_prefetch(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads,
+                                                 head_dim, rope_cos.as<float>(), rope_sin.as<float>(), cfg.context,
+                                                 kc, vc, slot_stride, head_stride, mixed.as<float>(), q_out,
+                                                 status.as<int32_t>(), &pf, stream));
       } else {
         Abi(accel_b200_rope_append(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads, head_dim,
                                    rope_cos.as<float>(), rope_sin.as<float>(), kc, vc, slot_stride, head_stride,

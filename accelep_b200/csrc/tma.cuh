@@ -54,6 +54,28 @@ __device__ __forceinline__ void BulkCopyG2S(void* dst, const void* src, uint32_t
       : "memory");
 }
 
+// The same copy with an L2 eviction policy (a createpolicy value).
+__device__ __forceinline__ void BulkCopyG2SHint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          SmemAddr(dst)),
+      "l"(src), "r"(bytes), "r"(SmemAddr(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 policy for data read once: evicted before other lines.
+__device__ __forceinline__ uint64_t EvictFirstPolicy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// Brings [src, src + bytes) into L2 (a hint; src and bytes multiples of 16).
+__device__ __forceinline__ void PrefetchL2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Non-blocking test of phase `parity`: the waiting thread is never suspended,
 // so a completed phase is seen on the next poll (a suspended try_wait adds a
 // wake-up delay to every hand-off of a pipeline).

@@ -258,15 +258,25 @@ def rope_append(qkv, row_seq, row_pos, heads, kv_heads, head_dim, cos_t, sin_t, 
 
 
 def decode_attention(qkv, row_pos, heads, kv_heads, cos_t, sin_t, k_cache, v_cache, row_seq=None, out=None,
-                     status=None):
+                     status=None, prefetch=None):
     """Fused decode step (Rope, AppendCache, attention) over un-rotated q|k|v
-    rows; caches head-major [slots, kv_heads, context, 64]."""
+    rows; caches head-major [slots, kv_heads, context, 64]. prefetch: up to
+    four contiguous device tensors to bring into L2 meanwhile (a hint)."""
     rows, ctx = qkv.shape[0], k_cache.shape[2]
     if out is None:
         out = torch.zeros(rows, heads * 64, dtype=torch.float32, device=qkv.device)
-    check(load().accel_b200_decode_attention(_p(qkv), qkv.stride(0), _p(row_seq), _p(row_pos), rows, heads, kv_heads,
-                                             64, _p(cos_t), _p(sin_t), ctx, _p(k_cache), _p(v_cache),
-                                             kv_heads * ctx * 64, ctx * 64, _p(out), out.stride(0), _p(status), _s()))
+    args = (_p(qkv), qkv.stride(0), _p(row_seq), _p(row_pos), rows, heads, kv_heads, 64, _p(cos_t), _p(sin_t), ctx,
+            _p(k_cache), _p(v_cache), kv_heads * ctx * 64, ctx * 64, _p(out), out.stride(0), _p(status))
+    if prefetch is None:
+        check(load().accel_b200_decode_attention(*args, _s()))
+    else:
+        from ._lib import L2Prefetch
+        pf = L2Prefetch()
+        for i, t in enumerate(prefetch):
+            pf.ptr[i] = t.data_ptr()
+            pf.bytes[i] = t.numel() * t.element_size()
+        pf.count = len(prefetch)
+        check(load().accel_b200_decode_attention_prefetch(*args, ctypes.byref(pf), _s()))
     return out
 
 

@@ -375,6 +375,26 @@ ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld,
                                                int64_t head_stride, float* out, int64_t out_ld, int32_t* status,
                                                void* stream);
 
+/* Up to four device ranges to bring into L2 (a hint: no completion, no
+   effect on results). */
+typedef struct accel_b200_l2_prefetch {
+  const void* ptr[4];
+  int64_t bytes[4];
+  int32_t count;
+} accel_b200_l2_prefetch;
+
+/* accel_b200_decode_attention that also brings `prefetch`'s ranges into L2
+   while it waits for its inputs and streams the cache (the engine passes the
+   weights of the layer's next products, which then read them from L2
+   instead of HBM). The cache rows are read with an evict-first L2 policy so
+   the stream of keys and values does not displace them. Results are those of
+   accel_b200_decode_attention. prefetch may be NULL. */
+ACCEL_B200_API int accel_b200_decode_attention_prefetch(
+    const float* qkv, int64_t qkv_ld, const int32_t* row_seq, const int32_t* row_pos, int64_t rows, int32_t heads,
+    int32_t kv_heads, int32_t head_dim, const float* cos_table, const float* sin_table, int32_t context,
+    float* k_cache, float* v_cache, int64_t seq_stride, int64_t head_stride, float* out, int64_t out_ld,
+    int32_t* status, const accel_b200_l2_prefetch* prefetch, void* stream);
+
 /* SiluMul (src/sim_silu.cc:8-13) over fused rows [gate (inter) | up (inter)]
    of row stride ld into out[r, i] (row stride ldo). */
 ACCEL_B200_API int accel_b200_silu_mul_rows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows,

@@ -104,6 +104,35 @@ def test_decode_attention_every_split_boundary(lib, cuda, orc):
         close(got[r], want.reshape(-1))
 
 
+def test_decode_attention_prefetch_same_results(lib, cuda):
+    """accel_b200_decode_attention_prefetch (L2 prefetch of other ranges, cache
+    rows read evict-first) writes the same outputs and cache bits as
+    accel_b200_decode_attention, and leaves the prefetched ranges alone."""
+    heads, kvh, hd, ctx = 9, 3, 64, 700
+    rng = np.random.default_rng(4)
+    pos = np.array([0, 63, 64, 699, -1, 300], np.int32)
+    rows = len(pos)
+    qkv = rng.standard_normal((rows, (heads + 2 * kvh) * hd), dtype=np.float32)
+    kc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    vc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    cos_t, sin_t = tables(ctx, hd)
+    weights = [torch.randint(-127, 128, (576, n), dtype=torch.int8, device="cuda") for n in (576, 3072, 100)]
+    before = [H(w).copy() for w in weights]
+    outs, caches = [], []
+    for pf in (None, weights):
+        kc_d, vc_d = T(kc), T(vc)
+        out = torch.full((rows, heads * hd), 7.0, device="cuda")
+        K.decode_attention(T(qkv), T(pos), heads, kvh, T(cos_t), T(sin_t), kc_d, vc_d, out=out, prefetch=pf)
+        outs.append(H(out))
+        caches.append((H(kc_d), H(vc_d)))
+    assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(caches[0][0], caches[1][0]) and np.array_equal(caches[0][1], caches[1][1])
+    for w, b in zip(weights, before):
+        assert np.array_equal(H(w), b)
+    with pytest.raises(B200Error):  # a range that is not 16-byte aligned
+        K.decode_attention(T(qkv), T(pos), heads, kvh, T(cos_t), T(sin_t), T(kc), T(vc), prefetch=[weights[0][0, 1:]])
+
+
 def test_decode_attention_rejects(lib, cuda):
     q = torch.zeros(2, 9 * 64 + 6 * 64, device="cuda")
     kc = torch.zeros(2, 3, 16, 64, device="cuda")

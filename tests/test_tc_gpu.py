@@ -174,3 +174,78 @@ def test_rmsnorm_from_sums_of_squares(lib, cuda, orc):
     np.testing.assert_allclose(by_sums, by_rows, rtol=1e-6, atol=1e-6)
     want = orc.execute_matmul_q(orc.rmsnorm(H(hid), H(gamma), m, h, 1e-5), w2, s2)
     np.testing.assert_allclose(by_sums, want, rtol=1e-4, atol=1e-4)
+
+
+# The integer tensor-core path puts each activation row segment in 30-bit fixed
+# point against its largest magnitude and sums the int8 digit planes exactly.
+# Shapes: in-kernel operand with and without split K, planes mode (long K walks
+# and m > 64).
+FIXED_POINT_SHAPES = [(32, 576, 256), (7, 256, 128), (16, 4096, 256), (100, 576, 384), (40, 1536, 128)]
+
+
+@pytest.mark.parametrize("m,k,n", FIXED_POINT_SHAPES)
+def test_power_of_two_scaling_is_exact(lib, cuda, m, k, n):
+    """Scaling the activations by 2^-60 or 2^40 scales every output by the
+    same power of two, bit for bit: the row exponents absorb the scale and the
+    digits do not change."""
+    x, w, s = syn.int8_gemm(m, k, n, m * 7 + k)
+    wt, st = T(w), T(s)
+    base = H(K.matmul_q8(T(x), wt, st))
+    for p in (-60, 40):
+        f = np.float32(2.0 ** p)
+        got = H(K.matmul_q8(T(x * f), wt, st))
+        assert np.array_equal(got, base * f), p
+
+
+@pytest.mark.parametrize("m,k,n", FIXED_POINT_SHAPES)
+def test_integer_activations_are_exact(lib, cuda, m, k, n):
+    """Integer-valued activations are represented exactly, so every output is
+    the exact integer dot product rounded once and times the column scale
+    (all partial sums stay below 2^24, so split-K adds are exact too)."""
+    rng = np.random.default_rng(k + n)
+    x = rng.integers(-16, 17, (m, k)).astype(np.float32)
+    w = rng.integers(-127, 128, (k, n)).astype(np.int8)
+    s = rng.uniform(1e-3, 1e-2, n).astype(np.float32)
+    got = H(K.matmul_q8(T(x), T(w), T(s)))
+    exact = x.astype(np.int64) @ w.astype(np.int64)
+    assert np.abs(exact).max() < 2 ** 24
+    want = exact.astype(np.float32) * s[None, :]
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("m,k,n", FIXED_POINT_SHAPES)
+def test_rows_of_different_magnitude(lib, cuda, orc, m, k, n):
+    """Rows whose magnitudes differ by 2^60 are each scaled by their own
+    exponent (every row keeps its precision), and a row with one element 2^20
+    times its others stays within the fixed point's bound: per element an
+    absolute error of at most 2^(e - 31)."""
+    x, w, s = syn.int8_gemm(m, k, n, m + 3 * k)
+    x = x.copy()
+    x[::2] *= np.float32(2.0 ** -60)
+    x[1, 3] = np.float32(2.0 ** 20)
+    got = H(K.matmul_q8(T(x), T(w), T(s)))
+    want = orc.execute_matmul_q(x, w, s)
+    ws = np.abs(w.astype(np.float64)) * s.astype(np.float64)
+    mag = np.abs(x).astype(np.float64) @ ws
+    # fp32 accumulation of the checker plus the fixed point's bound on each row
+    e = np.floor(np.log2(np.abs(x).max(axis=1).astype(np.float64))) + 1
+    fixed = (2.0 ** (e - 31))[:, None] * ws.sum(axis=0)[None, :]
+    tol = 2 * k * np.finfo(np.float32).eps * mag + fixed + 1e-30
+    err = np.abs(got.astype(np.float64) - want)
+    assert (err <= tol).all(), f"{(err > tol).sum()} outside, max ratio {(err / tol).max()}"
+
+
+def test_non_finite_rows_give_nan(lib, cuda):
+    """A row holding Inf or NaN yields NaN outputs; the other rows are the
+    same as without it."""
+    for m, k, n in [(32, 576, 256), (100, 576, 384)]:
+        x, w, s = syn.int8_gemm(m, k, n, 5)
+        wt, st = T(w), T(s)
+        base = H(K.matmul_q8(T(x), wt, st))
+        bad = x.copy()
+        bad[3, 10] = np.inf
+        bad[5, 0] = np.nan
+        got = H(K.matmul_q8(T(bad), wt, st))
+        assert np.isnan(got[3]).all() and np.isnan(got[5]).all()
+        keep = [r for r in range(m) if r not in (3, 5)]
+        assert np.array_equal(got[keep], base[keep])
