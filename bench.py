@@ -44,9 +44,9 @@ PROMPT_SEED = 41
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
 # DRAM bytes (read + write) per launch from ncu captures of the same launches
-# (profiles/q8_product_decode_qkv_m32.md: one decode step's products, 168.9 MB
+# (profiles/q8_product_decode_qkv_m32.md: one decode step's products, 168.2 MB
 # over 121 products; profiles/decode_attention_b32_len1280.md).
-PRODUCT_TRAFFIC = 1_395_815
+PRODUCT_TRAFFIC = 1_390_285
 ATTENTION_TRAFFIC = 63_610_368
 GEMV_TRAFFIC = 274_861_568  # profiles/q8_gemv_c5_m1_k16384.md
 
