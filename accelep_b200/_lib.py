@@ -79,6 +79,8 @@ SIGNATURES = {
                                              P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_matmul_q8_rmsnorm_stats": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_f32, P_plane, c_vp,
                                                    c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
+    "accel_b200_matmul_q8_rmsnorm_silu_pairs": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_f32, P_plane, c_vp,
+                                                        c_i64, c_i64, c_i64, c_i64, c_vp, c_sz, c_vp]),
     "accel_b200_matmul_f32_workspace": (c_sz, [c_i64, c_i64, c_i64]),
     "accel_b200_matmul_f32": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, P_ep, c_vp, c_sz, c_vp]),
     "accel_b200_rope_append": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,

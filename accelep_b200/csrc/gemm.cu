@@ -346,7 +346,7 @@ size_t TcWorkspace(int64_t m, int64_t k, int64_t n);
 int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
           const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
           const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream,
-          const PeerOut* peers, const double* sq_in, int64_t sq_ld, int32_t sq_n);
+          const PeerOut* peers, const double* sq_in, int64_t sq_ld, int32_t sq_n, bool silu_pairs);
 int LaunchRmsNormRows(const float* x, int64_t ldx, const float* w, float* y, int64_t ldy, int64_t rows, int64_t dim,
                       float eps, int64_t row_offset, cudaStream_t stream);
 int LaunchSiluMulRows(const float* gate_up, int64_t ld, float* out, int64_t ldo, int64_t rows, int64_t inter,
@@ -402,7 +402,7 @@ int MatMulQ8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c
   }
   if (UseTc(a, lda, w, b->axis, b->zero, m, k, n)) {
     return RunTc(a, nullptr, lda, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, k, n, g.ep, workspace,
-                 workspace_bytes, nullptr, AsStream(stream), peers, nullptr, 0, 0);
+                 workspace_bytes, nullptr, AsStream(stream), peers, nullptr, 0, 0, false);
   }
   if (with_peers || g.ep.row_sq != nullptr) {
     return SetError(ACCEL_B200_EINVAL,
@@ -513,7 +513,7 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
   if (inter % 4 == 0 && UseTc(gate_up, ld, w, b->axis, b->zero, m, inter, n) &&
       reinterpret_cast<uintptr_t>(up) % 16 == 0) {
     return RunTc(gate_up, up, ld, nullptr, 0.f, w, b->scale, b->axis < 0, c, ldc, m, inter, n, e, workspace,
-                 workspace_bytes, nullptr, AsStream(stream), nullptr, nullptr, 0, 0);
+                 workspace_bytes, nullptr, AsStream(stream), nullptr, nullptr, 0, 0, false);
   }
   // CUDA cores: SiluMul rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * inter * sizeof(float);
@@ -553,7 +553,7 @@ static int MatMulQ8RmsNorm(const float* x, int64_t ldx, const double* sq, int64_
   const int8_t* w = b->q + b->offset;
   if (UseTc(x, ldx, w, b->axis, b->zero, m, k, n) && reinterpret_cast<uintptr_t>(gamma) % 16 == 0) {
     return RunTc(x, nullptr, ldx, gamma, eps, w, b->scale, b->axis < 0, c, ldc, m, k, n, e, workspace,
-                 workspace_bytes, nullptr, AsStream(stream), nullptr, sq, sq_ld, sq_n);
+                 workspace_bytes, nullptr, AsStream(stream), nullptr, sq, sq_ld, sq_n, false);
   }
   // CUDA cores: RmsNorm rows into the workspace's tail, then the product.
   const size_t base = need - static_cast<size_t>(m) * k * sizeof(float);
@@ -581,6 +581,36 @@ ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm_stats(const float* x, int64_t ld
   }
   return MatMulQ8RmsNorm(x, ldx, row_sq, row_sq_ld, row_sq_n, gamma, eps, b, c, ldc, m, k, n, ep, workspace,
                          workspace_bytes, stream);
+}
+
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm_silu_pairs(const float* x, int64_t ldx, const double* row_sq,
+                                                           int64_t row_sq_ld, int32_t row_sq_n, const float* gamma,
+                                                           float eps, const accel_b200_q8_plane* b, float* c,
+                                                           int64_t ldc, int64_t m, int64_t k, int64_t n,
+                                                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 0 || k <= 0 || n <= 0 || n % 128 != 0 || b == nullptr || ldx < k || ldc < n / 2) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_rmsnorm_silu_pairs: out of range (n must be a multiple of 128)");
+  }
+  if (row_sq != nullptr && (row_sq_n <= 0 || row_sq_ld < row_sq_n)) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_rmsnorm_silu_pairs: bad row sums of squares");
+  }
+  if (m == 0) return ClearError();
+  if (x == nullptr || gamma == nullptr || c == nullptr || b->q == nullptr || b->scale == nullptr) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_rmsnorm_silu_pairs is missing an operand");
+  }
+  const int8_t* w = b->q + b->offset;
+  if (b->offset < 0 || !TcEligible(x, ldx, w, b->axis, b->zero, m, k, n) ||
+      reinterpret_cast<uintptr_t>(gamma) % 16 != 0) {
+    return SetError(ACCEL_B200_EINVAL,
+                    "matmul_q8_rmsnorm_silu_pairs: needs the tensor-core path (per-column or single scale, no zero "
+                    "points, k % 8 == 0, 16-byte aligned rows and gamma)");
+  }
+  if (workspace == nullptr || workspace_bytes < accel_b200_matmul_q8_rmsnorm_workspace(m, k, n)) {
+    return SetError(ACCEL_B200_EINVAL, "matmul_q8_rmsnorm_silu_pairs: workspace too small");
+  }
+  Epilogue e{};
+  return RunTc(x, nullptr, ldx, gamma, eps, w, b->scale, b->axis < 0, c, ldc, m, k, n, e, workspace, workspace_bytes,
+               nullptr, AsStream(stream), nullptr, row_sq, row_sq_ld, row_sq_n, true);
 }
 
 ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const float* b, float* c, int64_t ldc, int64_t m,

@@ -133,7 +133,8 @@ struct TcArgs {
   float* c;
   int64_t ldc;
   int32_t* status;
-  int32_t vec_store;  // c and ldc allow 16-byte row stores
+  int32_t vec_store;   // c and ldc allow 16-byte row stores
+  int32_t silu_pairs;  // gate|up columns in 64-column pairs; C = SiluMul(gate, up), n / 2 columns
   Epilogue ep;
   PeerOut peers;  // copies of C on other GPUs (n = 0: none)
 };
@@ -158,6 +159,32 @@ __device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int
 // SiluMul of one element as src/sim_silu.cc:8-13 rounds it.
 __device__ __forceinline__ float SiluMul(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+}
+
+// A gate|up product in 64-column pairs (TcArgs::silu_pairs: a 128-column
+// tile holds 64 gate columns, then the 64 up columns of the same outputs):
+// lanes l and l + 16 of a warp hold gate and up of the same output columns
+// (4l .. 4l + 3 of the tile), and lane l < 16 stores SiluMul of the pairs, as
+// SiluMul rounds it, at output columns n0 / 2 + 4l .. + 3 of the row.
+__device__ __forceinline__ void StoreSiluPairs(float* c, int64_t ldc, bool vec, int64_t row, int64_t n0, int lane,
+                                               float4 acc, const float (&sc)[4]) {
+  const float o[4] = {__fmul_rn(acc.x, sc[0]), __fmul_rn(acc.y, sc[1]), __fmul_rn(acc.z, sc[2]),
+                      __fmul_rn(acc.w, sc[3])};
+  float u[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) u[q] = __shfl_xor_sync(kFull, o[q], 16);
+  if (lane < 16) {
+    float* dst = c + row * ldc + n0 / 2 + 4 * lane;
+    const float4 y = make_float4(SiluMul(o[0], u[0]), SiluMul(o[1], u[1]), SiluMul(o[2], u[2]), SiluMul(o[3], u[3]));
+    if (vec) {
+      *reinterpret_cast<float4*>(dst) = y;
+    } else {
+      dst[0] = y.x;
+      dst[1] = y.y;
+      dst[2] = y.z;
+      dst[3] = y.w;
+    }
+  }
 }
 
 // ------------------------------------------------------------ fixed point
@@ -546,7 +573,12 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
       for (int j = 0; j < 4; ++j) {
         sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
       }
-      if (g.peers.n == 0 && g.ep.row_sq == nullptr && g.vec_store && cols == kBn) {
+      if (g.silu_pairs) {
+        for (int r = warp; r < rows; r += kThreads / 32) {
+          StoreSiluPairs(g.c, g.ldc, g.vec_store, row0 + r, n0, lane,
+                         *reinterpret_cast<const float4*>(tile + r * kBn + c4), sc);
+        }
+      } else if (g.peers.n == 0 && g.ep.row_sq == nullptr && g.vec_store && cols == kBn) {
         // The common case, kept free of the optional outputs.
 #pragma unroll 2
         for (int r = warp; r < rows; r += kThreads / 32) {
@@ -648,7 +680,9 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
 #pragma unroll
   for (int j = 0; j < kMaxJ; ++j) {
     const int r = r_begin + j * (kThreads / 32);  // the same for the 32 lanes of a warp
-    if (r < r_end) {
+    if (r < r_end && g.silu_pairs) {
+      StoreSiluPairs(g.c, g.ldc, g.vec_store, row0 + r, n0, lane, sum[j], sc);
+    } else if (r < r_end) {
       double sq = 0.0;
       if (c4 < cols) {
         const int64_t row = row0 + r;
@@ -903,12 +937,14 @@ size_t TcWorkspace(int64_t m, int64_t k, int64_t n) {
 
 // a: fp32 rows (lda); with `up` set, the product's A is SiluMul(a, up) (same
 // row stride); with `gamma` set, A is RmsNorm(a) with weights gamma [k] and
-// eps (a's rows are whole rows of length k). The caller checked TcEligible
-// for a (and up).
+// eps (a's rows are whole rows of length k). With silu_pairs, n % 128 == 0,
+// the weight columns are gate|up 64-column pairs and C receives SiluMul(gate,
+// up) (n / 2 columns; the epilogue is the plain product, no peers). The caller
+// checked TcEligible for a (and up).
 int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, float eps, const int8_t* w,
           const float* scale, bool scalar_scale, float* c, int64_t ldc, int64_t m, int64_t k, int64_t n,
           const Epilogue& ep, void* workspace, size_t workspace_bytes, int32_t* status, cudaStream_t stream,
-          const PeerOut* peers, const double* sq_in, int64_t sq_ld, int32_t sq_n) {
+          const PeerOut* peers, const double* sq_in, int64_t sq_ld, int32_t sq_n, bool silu_pairs) {
   const TcPlan p = MakeTcPlan(m, k, n, up != nullptr, gamma != nullptr);
   if (p.planes_bytes > 0 && (workspace == nullptr || workspace_bytes < kCounterRegion + p.planes_bytes)) {
     return SetError(ACCEL_B200_EINVAL, "matmul_q8: workspace too small");
@@ -988,6 +1024,7 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   g.ldc = ldc;
   g.status = status;
   g.vec_store = (reinterpret_cast<uintptr_t>(c) % 16 == 0 && ldc % 4 == 0) ? 1 : 0;
+  g.silu_pairs = silu_pairs ? 1 : 0;
   g.ep = ep;
   g.peers = peers != nullptr ? *peers : PeerOut{};
   for (int i = 0; i < g.peers.n; ++i) {

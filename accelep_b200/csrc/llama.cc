@@ -148,6 +148,9 @@ struct Group {
   DevBuf w;
   DevBuf scale;
   uint32_t loaded = 0;
+  // int8 gate|up stored in 64-column pairs (gate block t, then up block t):
+  // the product's epilogue then writes SiluMul(gate, up) directly.
+  bool paired = false;
 
   void Define(int64_t k_in, std::vector<int64_t> widths) {
     k = k_in;
@@ -289,14 +292,28 @@ class Engine {
       g->w.Alloc(static_cast<size_t>(g->k * g->n));
       g->scale.Alloc(static_cast<size_t>(g->n) * sizeof(float));
       g->kind = WKind::Q8;
+      g->paired = (kind == ACCEL_W_GATE || kind == ACCEL_W_UP) && cfg.intermediate % 64 == 0 && cfg.hidden % 8 == 0;
     }
     std::vector<int8_t> t(static_cast<size_t>(rows * cols));
     for (int64_t o = 0; o < rows; ++o)
       for (int64_t i = 0; i < cols; ++i) t[static_cast<size_t>(i * rows + o)] = q[o * cols + i];
-    Cuda(cudaMemcpy2D(g->w.as<int8_t>() + g->col0[member], g->n, t.data(), rows, rows, cols, cudaMemcpyHostToDevice),
-         "weight upload");
-    Cuda(cudaMemcpy(g->scale.as<float>() + g->col0[member], scale, rows * sizeof(float), cudaMemcpyHostToDevice),
-         "scale upload");
+    if (g->paired) {
+      // Block b of this member (gate: 0, up: 1) to columns 128 b + 64 member.
+      for (int64_t b = 0; b < rows / 64; ++b) {
+        Cuda(cudaMemcpy2D(g->w.as<int8_t>() + 128 * b + 64 * member, g->n, t.data() + 64 * b, rows, 64, cols,
+                          cudaMemcpyHostToDevice),
+             "weight upload");
+        Cuda(cudaMemcpy(g->scale.as<float>() + 128 * b + 64 * member, scale + 64 * b, 64 * sizeof(float),
+                        cudaMemcpyHostToDevice),
+             "scale upload");
+      }
+    } else {
+      Cuda(cudaMemcpy2D(g->w.as<int8_t>() + g->col0[member], g->n, t.data(), rows, rows, cols,
+                        cudaMemcpyHostToDevice),
+           "weight upload");
+      Cuda(cudaMemcpy(g->scale.as<float>() + g->col0[member], scale, rows * sizeof(float), cudaMemcpyHostToDevice),
+           "scale upload");
+    }
     NoteBytesToDevice(t.size() + rows * sizeof(float));
     g->loaded |= 1u << member;
     DropGraphs();
@@ -728,6 +745,15 @@ class Engine {
         }
       }
       Gemm(mixed.as<float>(), q_out, l.o, rows, hid, H, &residual);
+      if (l.gu.kind == WKind::Q8 && l.gu.paired) {
+        // RmsNorm -> gate|up -> SiluMul in one product, then the down product.
+        accel_b200_q8_plane plane{l.gu.w.as<int8_t>(), l.gu.scale.as<float>(), nullptr, 0, 1};
+        Abi(accel_b200_matmul_q8_rmsnorm_silu_pairs(hid, H, sq, SqBlocks(), static_cast<int32_t>(SqBlocks()),
+                                                    l.post_norm.as<float>(), cfg.eps, &plane, act.as<float>(), I,
+                                                    rows, H, 2 * I, gemm_ws.p, gemm_ws.bytes, stream));
+        Gemm(act.as<float>(), I, l.down, rows, hid, H, &residual);
+        continue;
+      }
       NormGemm(hid, l.post_norm, l.gu, rows, gu.as<float>(), 2 * I, nullptr, normed, sq);
       if (l.down.kind == WKind::Q8) {
         // SiluMul feeds the down projection's operand directly.

@@ -216,6 +216,34 @@ def matmul_q8_rmsnorm_stats(x, row_sq, gamma, eps, q, scale, axis=1, epilogue=No
     return c
 
 
+def pair_gate_up(gate_up, inter):
+    """Columns [gate (inter) | up (inter)] of a weight (or a scale vector) in
+    the 64-column pairs accel_b200_matmul_q8_rmsnorm_silu_pairs reads: block
+    t holds gate columns 64t .. 64t + 63, then the same up columns."""
+    lead = gate_up.shape[:-1]
+    g = gate_up[..., :inter].reshape(*lead, inter // 64, 64)
+    u = gate_up[..., inter:].reshape(*lead, inter // 64, 64)
+    return torch.stack([g, u], dim=-2).reshape(*lead, 2 * inter).contiguous()
+
+
+def matmul_q8_rmsnorm_silu_pairs(x, gamma, eps, q, scale, row_sq=None, axis=1, out=None, workspace=None):
+    """SiluMul(gate, up) of RmsNorm(x[:, :k]) @ dequant(q), q's columns in
+    64-column gate|up pairs (pair_gate_up); the result has n / 2 columns.
+    row_sq: optional [m, blocks] float64 sums of squares of x's rows."""
+    lib = load()
+    m = x.shape[0]
+    k, n = q.shape
+    c = out if out is not None else torch.zeros(m, n // 2, dtype=torch.float32, device=x.device)
+    plane = Q8Plane(q.data_ptr(), scale.data_ptr(), 0, 0, axis)
+    need = lib.accel_b200_matmul_q8_rmsnorm_workspace(m, k, n)
+    ws = workspace if workspace is not None else _workspace(x.device, need)
+    sq_ld, sq_n = (row_sq.stride(0), row_sq.shape[1]) if row_sq is not None else (0, 0)
+    check(lib.accel_b200_matmul_q8_rmsnorm_silu_pairs(_p(x), x.stride(0), _p(row_sq), sq_ld, sq_n, _p(gamma), eps,
+                                                      ctypes.byref(plane), _p(c), c.stride(0), m, k, n, _p(ws),
+                                                      0 if ws is None else ws.numel(), _s()))
+    return c
+
+
 def matmul_f32(a, b, epilogue=None, out=None):
     lib = load()
     m, k = a.shape

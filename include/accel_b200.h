@@ -252,6 +252,24 @@ ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm_stats(const float* x, int64_t ld
                                                       float eps, const accel_b200_q8_plane* b, float* c, int64_t ldc,
                                                       int64_t m, int64_t k, int64_t n, const accel_b200_epilogue* ep,
                                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* RmsNorm rows (as accel_b200_matmul_q8_rmsnorm; with row_sq non-NULL, from
+   the row sums of squares as accel_b200_matmul_q8_rmsnorm_stats) through a
+   fused gate|up product, then SiluMul (src/sim_silu.cc:8-13, the MLP of
+   src/llama_model.cc:237-240) in the product's epilogue. The plane's n
+   columns (n % 128 == 0) hold gate and up in 64-column pairs: columns
+   128 t .. 128 t + 63 are gate columns 64 t .. 64 t + 63 and columns
+   128 t + 64 .. 128 t + 127 the up columns of the same outputs. c[m, n / 2]
+   (row stride ldc) receives SiluMul(gate, up) of output columns 0 .. n / 2,
+   each value as the plain product followed by accel_b200_silu_mul_rows
+   computes it. Tensor-core path only (per-column or single scales, no zero
+   points, k % 8 == 0, 16-byte aligned rows and gamma); the workspace is
+   accel_b200_matmul_q8_rmsnorm_workspace(m, k, n). */
+ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm_silu_pairs(const float* x, int64_t ldx, const double* row_sq,
+                                                           int64_t row_sq_ld, int32_t row_sq_n, const float* gamma,
+                                                           float eps, const accel_b200_q8_plane* b, float* c,
+                                                           int64_t ldc, int64_t m, int64_t k, int64_t n,
+                                                           void* workspace, size_t workspace_bytes, void* stream);
 ACCEL_B200_API int accel_b200_matmul_q8_rmsnorm(const float* x, int64_t ldx, const float* gamma, float eps,
                                                 const accel_b200_q8_plane* b, float* c, int64_t ldc, int64_t m,
                                                 int64_t k, int64_t n, const accel_b200_epilogue* ep, void* workspace,

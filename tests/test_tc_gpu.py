@@ -10,6 +10,7 @@ import torch
 
 from accelep_b200 import kernels as K
 from accelep_b200 import synthetic as syn
+from accelep_b200._lib import B200Error
 
 pytestmark = pytest.mark.gpu
 
@@ -249,3 +250,43 @@ def test_non_finite_rows_give_nan(lib, cuda):
         assert np.isnan(got[3]).all() and np.isnan(got[5]).all()
         keep = [r for r in range(m) if r not in (3, 5)]
         assert np.array_equal(got[keep], base[keep])
+
+
+@pytest.mark.parametrize("m,k,inter,stats", [(32, 576, 1536, True), (32, 576, 1536, False), (7, 576, 256, False),
+                                             (200, 576, 384, False), (40, 1536, 128, True)])
+def test_rmsnorm_silu_pairs(lib, cuda, orc, m, k, inter, stats):
+    """The gate|up product with SiluMul in its epilogue
+    (accel_b200_matmul_q8_rmsnorm_silu_pairs, columns in 64-column pairs)
+    equals the plain RmsNorm-fed product of the unpaired columns followed by
+    SiluMul bit for bit; that product is within tolerance of the checker's
+    RmsNorm and MatMul."""
+    rng = np.random.default_rng(m + k + inter)
+    x = rng.standard_normal((m, k), dtype=np.float32) * 2
+    gamma = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    _, w, s = syn.int8_gemm(1, k, 2 * inter, m + inter)
+    xt, gt, wt, st = T(x), T(gamma), T(w), T(s)
+    sq = None
+    if stats:
+        blocks = (k + 127) // 128
+        x64 = x.astype(np.float64)
+        sq = T(np.stack([(x64[:, b * 128:(b + 1) * 128] ** 2).sum(axis=1) for b in range(blocks)], axis=1))
+    got = H(K.matmul_q8_rmsnorm_silu_pairs(xt, gt, 1e-5, K.pair_gate_up(wt, inter), K.pair_gate_up(st, inter),
+                                           row_sq=sq))
+    assert got.shape == (m, inter)
+    gu = (K.matmul_q8_rmsnorm_stats(xt, sq, gt, 1e-5, wt, st) if stats else K.matmul_q8_rmsnorm(xt, gt, 1e-5, wt, st))
+    gate, up = gu[:, :inter].contiguous(), gu[:, inter:].contiguous()
+    assert np.array_equal(got, H(K.silu_mul(gate, up)))
+    # The product part against the checker (fp32 accumulation bound), as the
+    # other product tests compare it.
+    normed = orc.rmsnorm(x, gamma, m, k, 1e-5)
+    mag = np.abs(normed).astype(np.float64) @ (np.abs(w.astype(np.float64)) * s.astype(np.float64))
+    check_close(H(gu), orc.execute_matmul_q(normed, w, s), k, mag)
+
+
+def test_rmsnorm_silu_pairs_rejects(lib, cuda):
+    x = torch.zeros(4, 576, device="cuda")
+    g = torch.ones(576, device="cuda")
+    w = torch.zeros(576, 200, dtype=torch.int8, device="cuda")
+    s = torch.ones(200, device="cuda")
+    with pytest.raises(B200Error):  # n not a multiple of 128
+        K.matmul_q8_rmsnorm_silu_pairs(x, g, 1e-5, w, s)
