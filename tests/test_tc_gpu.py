@@ -86,7 +86,7 @@ def test_tc_scalar_scale_and_repeat(lib, cuda, orc):
                                        (7, 100, 336)])
 def test_silu_product_matches_checker(lib, cuda, orc, m, inter, n):
     """SiluMul rows feeding the product (accel_b200_matmul_q8_silu): the
-    in-kernel SiluMul of the fp32-tile path (m <= 64), the split pass of the
+    in-kernel SiluMul (m <= 64, up to two k blocks per CTA), the digit pass of the
     planes path (m > 64), and the CUDA-core path (inter not a multiple of 4
     or 8 goes there too), each against SiluMul + MatMul of the checker."""
     rng = np.random.default_rng(m * inter + n)
@@ -104,7 +104,7 @@ def test_silu_product_matches_checker(lib, cuda, orc, m, inter, n):
 
 
 def test_fp32_tile_product_every_row_count(lib, cuda, orc):
-    """m = 1 .. 64 on the fp32-tile path (R = 16, 32 and 64, ragged row tiles)."""
+    """m = 1 .. 64 with the in-kernel operand (R = 16, 32 and 64, ragged row tiles)."""
     x, w, s = syn.int8_gemm(64, 576, 256, 11)
     xt, wt, st = T(x), T(w), T(s)
     want = orc.execute_matmul_q(x, w, s)
@@ -118,7 +118,7 @@ def test_fp32_tile_product_every_row_count(lib, cuda, orc):
                                        (100, 576, 384, 576), (1, 1536, 256, 1536), (7, 100, 336, 100)])
 def test_rmsnorm_product(lib, cuda, orc, m, k, n, ldx):
     """RmsNorm rows feeding the product (accel_b200_matmul_q8_rmsnorm): the
-    in-kernel norm of the fp32-tile path, the norm pass of the planes path
+    in-kernel norm (decode sizes), the norm variant of the digit pass (planes mode)
     (long K walks, m > 64) and the CUDA-core path (k % 8 != 0). The
     normalized values are those of accel_b200_rmsnorm, so the result equals
     RmsNorm then the product bit for bit, and the checker's RmsNorm + MatMul
