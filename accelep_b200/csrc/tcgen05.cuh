@@ -1,7 +1,6 @@
 // 5th-generation tensor core (tcgen05) helpers in inline PTX for sm_100a:
-// TMEM allocation, shared-memory matrix descriptors, the bf16 MMA with fp32
-// accumulation and the int8 MMA with int32 accumulation in TMEM, commit to an
-// mbarrier, and TMEM loads.
+// TMEM allocation, shared-memory matrix descriptors, the int8 MMA with int32
+// accumulation in TMEM, commit to an mbarrier, and TMEM loads.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -46,18 +45,6 @@ __device__ __forceinline__ uint64_t SmemDescSw128(uint32_t saddr, uint32_t lbo_b
   return d;
 }
 
-// Instruction descriptor of kind::f16 with bf16 A and B, fp32 D, M = 128.
-// a_mn_major: A stored M-contiguous; B is K-major. n: the MMA N (16..256, % 16).
-__host__ __device__ constexpr uint32_t InstrDescBf16(uint32_t n, bool a_mn_major) {
-  return (1u << 4)                            // D format: f32
-         | (1u << 7)                          // A format: bf16
-         | (1u << 10)                         // B format: bf16
-         | ((a_mn_major ? 1u : 0u) << 15)     // A major
-         | (0u << 16)                         // B major: K
-         | ((n >> 3) << 17)                   // N >> 3
-         | ((128u >> 4) << 24);               // M >> 4
-}
-
 // Instruction descriptor of kind::i8 with signed int8 A and B, int32 D,
 // M = 128; A stored M-contiguous (MN-major), B K-major. n: the MMA N (16..256, % 16).
 __host__ __device__ constexpr uint32_t InstrDescS8(uint32_t n) {
@@ -81,57 +68,12 @@ __device__ __forceinline__ void MmaS8(uint32_t tmem_d, uint64_t adesc, uint64_t 
       : "memory");
 }
 
-// D[tmem] (+)= A[smem] x B[smem], issued by one thread.
-__device__ __forceinline__ void MmaBf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // Arrives on `bar` once every tensor-core operation this thread issued so far
 // has completed.
 __device__ __forceinline__ void MmaCommit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
                : "memory");
-}
-
-// 32 consecutive fp32 columns of this thread's TMEM lane (32x32b shape: warp w
-// reads lanes 32w .. 32w + 31).
-__device__ __forceinline__ void TmemLoad32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// 16 consecutive fp32 columns of this thread's TMEM lane (32x32b shape).
-__device__ __forceinline__ void TmemLoad16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // 16 consecutive 32-bit columns of this thread's TMEM lane, raw, without
