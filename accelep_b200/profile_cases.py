@@ -72,11 +72,14 @@ def gemm_case(name, m, k, n, reps, copies=None):
 
 
 def decode_products(batch=32, layers=30, hidden=576, inter=1536, q_out=576, kv_out=192, vocab=49152, seed=5):
-    """The int8 products of one decode step of the C4 model, issued as the
-    engine issues them: per layer the fused q|k|v projection fed by RmsNorm
-    rows, the output projection (+ residual), the fused gate|up projection fed
-    by RmsNorm rows and the down projection fed by SiluMul rows (+ residual),
-    then the LM head fed by RmsNorm rows; synthetic weights of the same shapes.
+    """The int8 products of one decode step of the C4 model at its shapes:
+    per layer the fused q|k|v projection fed by RmsNorm rows, the output
+    projection (+ residual), the fused gate|up projection fed by RmsNorm rows
+    and the down projection fed by SiluMul rows (+ residual), then the LM head
+    fed by RmsNorm rows; synthetic weights of the same shapes. (The engine
+    stores gate|up in column pairs and applies SiluMul in the gate|up
+    epilogue, so its down product reads the activations directly; the
+    product count and weight bytes are the same.)
     Returns (launch(i), algorithmic bytes per step, launches per step): the
     algorithmic bytes of a product are its int8 weights, scales, fp32 A rows
     read, C rows written and residual rows read."""
