@@ -19,7 +19,7 @@
 // of at most 2^(e - 31) otherwise. X is written as four balanced base-256 digits
 // (int8, X = d0 2^24 + d1 2^16 + d2 2^8 + d3), the four digit planes are the
 // MMA's B operand, and the tensor core sums w * d exactly in int32 (|sum| <
-// 2^31 for up to 2^17 k per CTA). The epilogue recombines the planes in int64,
+// 2^31 for up to 1023 * 128 k per CTA). The epilogue recombines the planes in int64,
 // rounds once to fp32 and scales by 2^(e - 30): the result is the correctly
 // rounded dot product of the weights with the fixed-point row, which is no
 // further from the exact product than the reference's own fp32 accumulation.
@@ -86,7 +86,7 @@ constexpr int kWBytes = kBk * kBn;      // int8 weight block, 16 KiB
 constexpr int kDigits = 4;              // int8 digits per fixed-point activation
 constexpr int kExpMin = -96;            // smallest row exponent: keeps 2^(30 - e) a normal float
 constexpr int32_t kBadRow = 0x7fff;     // exponent of a row holding Inf or NaN
-constexpr int kMaxBlocksPerCta = 1024;  // 2^17 k: int32 sums of int8 x int8 cannot overflow
+constexpr int kMaxBlocksPerCta = 1023;  // |w d| <= 2^14, so 1023 * 128 k of them sum below 2^31
 constexpr int kInKernelBlocks = 2;      // k blocks of a CTA that forms its own operand
 // Converter warps: eight where they form the operand (latency-bound decode
 // products: more threads shorten the operand and epilogue work) and where the
@@ -918,7 +918,7 @@ bool Encode2D(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint
 // Whether the tensor-core path takes this product: a per-column or single
 // scale without zero points; weight rows a multiple of 16 bytes (TMA stride)
 // and activation rows a multiple of 8 elements; 16-byte aligned; at most 8 x
-// 2^17 k (the int32 sums of a CTA hold 2^17 k).
+// 1023 * 128 k (the int32 sums of a CTA hold 1023 * 128 k).
 bool TcEligible(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
                 int64_t n) {
   if (zero != nullptr || (axis != 1 && axis != -1)) return false;
