@@ -15,6 +15,7 @@
 // The reference divides each weight by the sum before the value product;
 // here the sum divides the accumulated product once. The two orders agree
 // well inside the 1e-4 tolerance.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -361,29 +362,100 @@ static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchB
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchSlot {
+  unsigned long long context_id = 0;  // the CUDA context the address belongs to
+  void* address = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// The unique id of the current CUDA context (the driver's cuCtxGetId, reached
+// through the runtime's entry-point query, so the library needs no libcuda at
+// link time). A device reset ends the context; the next one has another id.
+int CurrentContextId(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  if (get_current == nullptr || get_id == nullptr) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1{}, q2{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess || f1 == nullptr ||
+        f2 == nullptr) {
+      cudaGetLastError();
+      return SetError(ACCEL_B200_ECUDA, "noalloc scratch: the driver does not offer cuCtxGetId");
+    }
+    get_current = reinterpret_cast<CtxGetCurrentFn>(f1);
+    get_id = reinterpret_cast<CtxGetIdFn>(f2);
+  }
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS) {
+    return SetError(ACCEL_B200_ECUDA, "noalloc scratch: no current CUDA context");
+  }
+  return ACCEL_B200_OK;
+}
 
 // The device address of the scratch array on the current device. In host code
 // g_decode_scratch names a host-side stand-in, not device memory: a kernel
 // given that name would fault or read the wrong memory, so the address is
-// looked up once per device and cached.
+// looked up with cudaGetSymbolAddress once per device (and again after a
+// device reset, which gives the device a new context) and cached.
 int ScratchAddress(void** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return SetError(ACCEL_B200_ECUDA, std::string("noalloc scratch: ") + cudaGetErrorString(err));
   if (dev < 0 || dev >= kMaxDevices) return SetError(ACCEL_B200_EINVAL, "noalloc scratch: device ordinal above 63");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* ptr = nullptr;
-    err = cudaGetSymbolAddress(&ptr, g_decode_scratch);
-    if (err != cudaSuccess || ptr == nullptr) {
-      cudaGetLastError();
-      return SetError(ACCEL_B200_ECUDA, std::string("noalloc scratch: cudaGetSymbolAddress failed: ") +
-                                            cudaGetErrorString(err));
+  ScratchSlot& slot = g_scratch[dev];
+  unsigned long long ctx_id = 0;
+  if (slot.address != nullptr) {
+    // Cheap check that the cached address still belongs to the live context.
+    const int rc = CurrentContextId(&ctx_id);
+    if (rc != ACCEL_B200_OK) return rc;
+    if (ctx_id == slot.context_id) {
+      *out = slot.address;
+      return ACCEL_B200_OK;
     }
-    g_scratch_addr[dev] = ptr;
   }
-  *out = g_scratch_addr[dev];
+  void* ptr = nullptr;
+  err = cudaGetSymbolAddress(&ptr, g_decode_scratch);  // also creates the context on first use
+  if (err != cudaSuccess || ptr == nullptr) {
+    cudaGetLastError();
+    return SetError(ACCEL_B200_ECUDA, std::string("noalloc scratch: cudaGetSymbolAddress failed: ") +
+                                          cudaGetErrorString(err));
+  }
+  const int rc = CurrentContextId(&ctx_id);
+  if (rc != ACCEL_B200_OK) return rc;
+  slot.address = ptr;
+  slot.context_id = ctx_id;
+  *out = ptr;
+  return ACCEL_B200_OK;
+}
+
+// The argument checks of the split-KV decode attention, shared by the
+// workspace and the no-allocation entry points, so that both reject a bad
+// call before anything is queued on the stream.
+int CheckDecodeArgs(const float* q, const float* k, const float* v, int64_t kv_row_stride, int64_t kv_head_stride,
+                    int64_t kv_seq_stride, const int32_t* lens, int32_t batch, int32_t heads, int32_t kv_heads,
+                    int32_t head_dim, int32_t max_len, int32_t chunk, const float* out) {
+  if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim != kDecD || max_len <= 0 ||
+      chunk <= 0 || chunk > 128 || lens == nullptr || q == nullptr || k == nullptr || v == nullptr || out == nullptr) {
+    return SetError(ACCEL_B200_EINVAL, "attention_decode: bad arguments");
+  }
+  if (heads / kv_heads > kMaxGroup) {
+    return SetError(ACCEL_B200_EINVAL, "attention_decode: more than 8 query heads per kv head");
+  }
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16 != 0 || kv_row_stride % 4 != 0 ||
+      kv_head_stride % 4 != 0 || kv_seq_stride % 4 != 0) {
+    return SetError(ACCEL_B200_EINVAL, "attention_decode: cache rows must be 16-byte aligned");
+  }
+  // One arrival counter per (sequence, kv head) in the workspace's fixed
+  // counter region.
+  if (static_cast<int64_t>(batch) * kv_heads > kMaxCounters) {
+    return SetError(ACCEL_B200_EINVAL, "attention_decode: batch * kv_heads above 16384");
+  }
   return ACCEL_B200_OK;
 }
 }  // namespace
@@ -450,17 +522,11 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
                                                int32_t head_dim, int32_t max_len, int32_t chunk, float* out,
                                                int64_t out_row_stride, void* workspace, size_t workspace_bytes,
                                                int32_t* status, void* stream) {
-  if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || head_dim != kDecD || max_len <= 0 ||
-      chunk <= 0 || chunk > 128 || lens == nullptr || q == nullptr || k == nullptr || v == nullptr || out == nullptr) {
-    return SetError(ACCEL_B200_EINVAL, "attention_decode: bad arguments");
-  }
+  const int rc = CheckDecodeArgs(q, k, v, kv_row_stride, kv_head_stride, kv_seq_stride, lens, batch, heads, kv_heads,
+                                 head_dim, max_len, chunk, out);
+  if (rc != ACCEL_B200_OK) return rc;
   if (batch == 0) return ClearError();
   const int group = heads / kv_heads;
-  if (group > kMaxGroup) return SetError(ACCEL_B200_EINVAL, "attention_decode: more than 8 query heads per kv head");
-  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16 != 0 || kv_row_stride % 4 != 0 ||
-      kv_head_stride % 4 != 0 || kv_seq_stride % 4 != 0) {
-    return SetError(ACCEL_B200_EINVAL, "attention_decode: cache rows must be 16-byte aligned");
-  }
   const size_t need = accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk);
   if (workspace == nullptr || workspace_bytes < need) return SetError(ACCEL_B200_EINVAL, "attention_decode: workspace too small");
   DecodeArgs a{};
@@ -477,9 +543,6 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
   a.chunk = chunk;
   a.n_chunks = (max_len + chunk - 1) / chunk;
   a.scale = 1.f / sqrtf(static_cast<float>(head_dim));
-  if (static_cast<int64_t>(batch) * kv_heads > kMaxCounters) {
-    return SetError(ACCEL_B200_EINVAL, "attention_decode: batch * kv_heads above 16384");
-  }
   a.counters = static_cast<int32_t*>(workspace);
   a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegion);
   a.status = status;
@@ -506,6 +569,12 @@ ACCEL_B200_API int accel_b200_attention_decode_noalloc(const float* q, int64_t q
                                                        int32_t heads, int32_t kv_heads, int32_t head_dim,
                                                        int32_t max_len, int32_t chunk, float* out,
                                                        int64_t out_row_stride, int32_t* status, void* stream) {
+  // Every argument is checked before the scratch is touched: a call that
+  // fails here queues nothing.
+  int rc = CheckDecodeArgs(q, k, v, kv_row_stride, kv_head_stride, kv_seq_stride, lens, batch, heads, kv_heads,
+                           head_dim, max_len, chunk, out);
+  if (rc != ACCEL_B200_OK) return rc;
+  if (batch == 0) return ClearError();
   const size_t need = accel_b200_attention_decode_workspace(batch, heads, kv_heads, max_len, chunk);
   if (need > kNoAllocScratchBytes) {
     return SetError(ACCEL_B200_EINVAL,
@@ -513,16 +582,15 @@ ACCEL_B200_API int accel_b200_attention_decode_noalloc(const float* q, int64_t q
                         " bytes of scratch, above the fixed 4 MiB (4194304 bytes); use accel_b200_attention_decode "
                         "with a caller-owned workspace");
   }
-  if (batch <= 0) return accel_b200_attention_decode(q, q_row_stride, k, v, kv_row_stride, kv_head_stride,
-                                                     kv_seq_stride, lens, batch, heads, kv_heads, head_dim, max_len,
-                                                     chunk, out, out_row_stride, nullptr, 0, status, stream);
   void* scratch = nullptr;
-  const int rc = ScratchAddress(&scratch);
+  rc = ScratchAddress(&scratch);
   if (rc != ACCEL_B200_OK) return rc;
-  // The array keeps whatever the last call left; the arrival counters must
-  // start at zero, so they are cleared on this call's stream first.
-  const cudaError_t err =
-      cudaMemsetAsync(scratch, 0, static_cast<size_t>(batch) * kv_heads * sizeof(int32_t), AsStream(stream));
+  // The array keeps whatever the last call left; the arrival counters (one
+  // per (sequence, kv head), at most the counter region) must start at zero,
+  // so they are cleared on this call's stream first.
+  const size_t counter_bytes = static_cast<size_t>(batch) * kv_heads * sizeof(int32_t);
+  const cudaError_t err = cudaMemsetAsync(scratch, 0, counter_bytes < kCounterRegion ? counter_bytes : kCounterRegion,
+                                          AsStream(stream));
   if (err != cudaSuccess) {
     return SetError(ACCEL_B200_ECUDA, std::string("attention_decode_noalloc: ") + cudaGetErrorString(err));
   }

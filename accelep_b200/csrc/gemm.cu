@@ -361,19 +361,20 @@ int RunGemv(const float* a, int64_t lda, const int8_t* w, const float* scale, bo
 
 namespace {
 // 0: by shape (GEMV for m <= 8, tensor cores above), 1: CUDA cores,
-// 2: tensor cores where eligible, 3: GEMV where eligible.
-std::atomic<int> g_q8_path{0};
+// 2: tensor cores where eligible, 3: GEMV where eligible. Per thread: a
+// choice made on one thread never changes the products another thread runs.
+thread_local int g_q8_path = 0;
 
 bool UseTc(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
            int64_t n) {
-  const int path = g_q8_path.load(std::memory_order_relaxed);
+  const int path = g_q8_path;
   if (path == 1 || path == 3) return false;
   return TcEligible(a, lda, w, axis, zero, m, k, n);
 }
 
 bool UseGemv(const float* a, int64_t lda, const int8_t* w, int32_t axis, const int8_t* zero, int64_t m, int64_t k,
              int64_t n) {
-  const int path = g_q8_path.load(std::memory_order_relaxed);
+  const int path = g_q8_path;
   if (path == 1 || path == 2) return false;
   return GemvEligible(a, lda, w, axis, zero, m, k, n);
 }
@@ -451,7 +452,7 @@ ACCEL_B200_API int accel_b200_set_q8_path(int32_t path) {
   if (path < 0 || path > 3) {
     return SetError(ACCEL_B200_EINVAL, "set_q8_path: 0 (by shape), 1 (CUDA cores), 2 (tensor cores), 3 (GEMV)");
   }
-  g_q8_path.store(path, std::memory_order_relaxed);
+  g_q8_path = path;
   return ClearError();
 }
 

@@ -4,18 +4,25 @@
 // The reference runs a forward as 17 device calls per layer on one
 // sequence. Here a forward runs over a set of rows that may belong to many
 // sequences (a prefill of several prompts, or one new token per sequence in
-// decode), and the layer is 8 launches:
+// decode). With int8 weights a decode layer is 5 launches:
 //
-//   RmsNorm -> one q|k|v product -> RoPE + cache append -> attention ->
-//   o product with the residual add fused -> RmsNorm -> one gate|up product
-//   -> SiLU-mul -> down product with the residual add fused
+//   q|k|v product (RmsNorm fused into its operand) -> fused RoPE + cache
+//   append + attention -> o product (residual add fused) -> gate|up product
+//   (RmsNorm fused into its operand, SiluMul into its epilogue) -> down
+//   product (residual add fused)
+//
+// and a prefill layer adds the separate RoPE + append and the tiled prefill
+// attention in place of the fused decode attention.
 //
 // Linear weights live in HBM in the reference's device layout [in, out]
 // (src/llama_model.cc:75-84 transposes Hugging Face [out, in]); q, k and v of
 // a layer share one [hidden, q + 2 kv] matrix and gate and up one
 // [hidden, 2 intermediate] matrix, so each is one product. A weight is fp32
-// or int8 with a per-output scale. The KV cache is fp32 [slot][context][kv
-// heads][head_dim] per layer, the reference's per-sequence layout.
+// or int8 with a per-output scale. The KV cache is fp32 and head-major,
+// [slot][kv head][context][head_dim] per layer, so one (sequence, kv head)
+// run of rows is contiguous for the decode kernel's bulk copies;
+// accel_llama_cache_rows returns rows in the reference's [context][kv
+// heads][head_dim] layout.
 //
 // Decode: the step (choose the next id of every live sequence, then one
 // forward of one row per sequence) is captured once as a CUDA graph and
@@ -353,6 +360,7 @@ class Engine {
     Forward(count, 1, false);
     Cuda(cudaStreamSynchronize(stream), "forward");
     filled += count;
+    logit_rows = 1;
   }
 
   // src/llama_model.cc:101-131, for `batch` sequences at once.
@@ -423,6 +431,7 @@ class Engine {
     Cuda(cudaMemsetAsync(count.p, 0, batch * 4, stream), "state");
     Cuda(cudaMemsetAsync(step.p, 0, 16, stream), "state");
     Forward(rows, batch, false);
+    logit_rows = batch;
 
     cudaGraphExec_t exec = steps > 0 ? StepGraph(batch, sampled, temperature, top_k, eos) : nullptr;
     PinnedBuf& fin = finished_host;
@@ -456,9 +465,11 @@ class Engine {
       filled = len0;
     } else {
       const int64_t width = std::max(1, max_new);
-      Cuda(cudaMemcpy2D(out_ids, width * 4, ids.p, ids_stride * 4, static_cast<size_t>(std::max(steps, 0)) * 4, batch,
-                        cudaMemcpyDeviceToHost),
-           "ids");
+      if (steps > 0) {
+        Cuda(cudaMemcpy2D(out_ids, width * 4, ids.p, ids_stride * 4, static_cast<size_t>(steps) * 4, batch,
+                          cudaMemcpyDeviceToHost),
+             "ids");
+      }
       NoteBytesToHost(static_cast<size_t>(batch) * std::max(steps, 0) * 4);
       filled = 0;
     }
@@ -478,8 +489,12 @@ class Engine {
     return host;
   }
 
+  // One row per sequence of the last forward (n = rows * vocab); after a
+  // batched generate, row b is sequence b's last forward.
   void Logits(float* out, int32_t n) {
-    if (out == nullptr || n != cfg.vocab) throw std::invalid_argument("invalid logit buffer");
+    if (out == nullptr || n <= 0 || n % cfg.vocab != 0 || n / cfg.vocab > logit_rows) {
+      throw std::invalid_argument("invalid logit buffer");
+    }
     Cuda(cudaMemcpyAsync(out, logits.p, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, stream), "logits");
     Cuda(cudaStreamSynchronize(stream), "logits");
   }
@@ -505,6 +520,7 @@ class Engine {
   int device = 0;
   int32_t head_dim = 0, q_out = 0, kv_out = 0;
   int32_t filled = 0;
+  int32_t logit_rows = 0;  // logit rows the last forward wrote
   cudaStream_t stream = nullptr;
   std::mutex mu;
 

@@ -1,9 +1,12 @@
 // Bulk-copy (TMA) and mbarrier helpers in inline PTX for sm_100a.
 //
-// Only the untiled global -> shared bulk copy is used here, with a CTA-local
-// destination and no cluster multicast: every copy reads this GPU's own
-// memory into this CTA's shared memory. Waits on an mbarrier are bounded;
-// a wait that runs out reports failure to its caller instead of spinning on.
+// This header holds the untiled global -> shared bulk copy and the L2
+// prefetch; the tiled tensor-map copies (cp.async.bulk.tensor) of the
+// tensor-core product live in gemm_tc.cu. Every copy in this library has a
+// CTA-local destination and no cluster multicast: it reads this GPU's own
+// memory into the issuing CTA's shared memory. Waits on an mbarrier are
+// bounded; a wait that runs out reports failure to its caller instead of
+// spinning on.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -122,8 +122,11 @@ class Llama:
                     "logit max abs")
         return float(out[0])
 
-    def logits(self):
-        out = np.zeros(self.cfg["vocab"], dtype=np.float32)
+    def logits(self, rows=None):
+        """The last forward's logit row, or with `rows` its first `rows` rows
+        (one per sequence of a batched generate) as [rows, vocab]."""
+        shape = (self.cfg["vocab"],) if rows is None else (rows, self.cfg["vocab"])
+        out = np.zeros(shape, dtype=np.float32)
         self._check(self._lib.accel_llama_logits(self._model, _ptr(out, P_f32), out.size), "logits")
         return out
 

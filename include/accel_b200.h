@@ -165,11 +165,13 @@ typedef struct accel_b200_epilogue {
 /* Scratch, in bytes, accel_b200_matmul_q8 needs for these sizes. */
 ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64_t n);
 
-/* Which kernel accel_b200_matmul_q8 uses, process-wide: 0 by shape (the
-   default: for per-column or single scales without zero points and 16-byte
-   aligned rows, the int8 GEMV for m <= 8 and the tcgen05 tensor-core kernel
-   above; CUDA cores otherwise), 1 CUDA cores only, 2 the tensor-core kernel
-   where eligible, 3 the GEMV where eligible. For comparisons and tests. */
+/* Which kernel the int8 products launched FROM THE CALLING THREAD use: 0 by
+   shape (the default: for per-column or single scales without zero points
+   and 16-byte aligned rows, the int8 GEMV for m <= 8 and the tcgen05
+   tensor-core kernel above; CUDA cores otherwise), 1 CUDA cores only, 2 the
+   tensor-core kernel where eligible, 3 the GEMV where eligible. The choice is
+   thread-local: products launched by other threads (another model, another
+   device) keep the by-shape choice. For comparisons and tests. */
 ACCEL_B200_API int accel_b200_set_q8_path(int32_t path);
 
 /* src/sim_device.cc:541-602 (MatMulQuantized with a right-hand plane) and
@@ -357,12 +359,14 @@ ACCEL_B200_API int accel_b200_attention_decode(const float* q, int64_t q_row_str
    device memory (accel_b200_attention_decode_noalloc_limit() bytes; each GPU
    that loads the library holds it until the process exits); sizes whose
    workspace would exceed it are rejected with ACCEL_B200_EINVAL. The entry
-   point calls no cudaMalloc, cudaFree or allocating library routine. The
-   first call on a device looks up the array's device address with
-   cudaGetSymbolAddress, so make that first call before any stream capture.
-   All calls share the array and each clears the arrival counters it needs on
-   its own stream; calls that overlap on the GPU (different streams, several
-   threads) race on the array. */
+   point calls no cudaMalloc, cudaFree or allocating library routine. Every
+   argument is checked before the array is touched; a rejected call queues
+   nothing. The first call on a device (and the first after a device reset,
+   which gives the device a new context) looks up the array's device address
+   with cudaGetSymbolAddress, so make that first call before any stream
+   capture. All calls share the array and each clears the arrival counters it
+   needs on its own stream; calls that overlap on the GPU (different streams,
+   several threads) race on the array. */
 ACCEL_B200_API size_t accel_b200_attention_decode_noalloc_limit(void);
 ACCEL_B200_API int accel_b200_attention_decode_noalloc(const float* q, int64_t q_row_stride, const float* k,
                                                        const float* v, int64_t kv_row_stride, int64_t kv_head_stride,

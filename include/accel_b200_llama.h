@@ -132,7 +132,9 @@ ACCEL_B200_API int accel_llama_complete_stream(AccelLlama* model, const char* pr
 ACCEL_B200_API int accel_llama_forward_ids(AccelLlama* model, const int32_t* ids, int32_t count, int32_t reset);
 ACCEL_B200_API int accel_llama_logit_max_abs(AccelLlama* model, const float* reference, int32_t count,
                                              float* out_max_abs);
-/* Copies the current logit row (vocab floats) to the host. Test hook; not counted. */
+/* Copies the logit rows of the last forward to the host: count = r * vocab
+   floats give rows 0..r-1 (one per sequence of the last forward or batched
+   generate, in slot order). Test hook; not counted. */
 ACCEL_B200_API int accel_llama_logits(AccelLlama* model, float* out, int32_t count);
 /* Copies rows [0, rows) of one layer's key (which 0) or value (which 1) cache
    of sequence slot `slot` to the host in the reference layout [rows,

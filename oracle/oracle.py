@@ -17,7 +17,9 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libaccel_ref.so"
-REF_SOURCES = Path(os.environ.get("ACCEL_REF_ROOT", "/root/reference"))
+# The AccelEP checkout the reference library is built from: ACCEL_REF_ROOT,
+# else a directory named `reference` beside this repository's root.
+REF_SOURCES = Path(os.environ.get("ACCEL_REF_ROOT", str(HERE.parent.parent / "reference")))
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int32)

@@ -18,6 +18,11 @@ Outputs:
                     int8 weights; long, so the restatement runs it, after
                     the restatement was pinned bit for bit against the
                     reference on the first sequence's opening steps)
+  c4_logits.npz     C4 (--c4-logits): logit rows of two greedy sequences (fed
+                    the golden ids) and two sampled ones (temperature 1, full
+                    vocabulary) after the prefill and after 513 and 1536
+                    decode forwards, with the sampled ids; the sampled loop is
+                    pinned against the reference's Generate on 8 ids
 """
 
 import argparse
@@ -270,11 +275,95 @@ def make_c4(ref, orc, workers):
     return {"prompts_sha": np.frombuffer(bytes.fromhex(sha(prompts)), np.uint8), "ids": ids, "gaps": gaps}
 
 
+# Decode forwards after the prefill at which C4 logit rows are kept: 0 (the
+# prefill's last row, position 511), 513 (position 1024) and 1536 (position
+# 2047, the last row of the 2048-row context).
+C4_LOGIT_STEPS = (0, 513, 1536)
+C4_GREEDY_SEQS = (0, 17)
+C4_SAMPLED_SEQS = (3, 29)
+C4_TEMPERATURE = 1.0
+
+
+def c4_seed(b):
+    """Seed of sampled sequence b in the C4 logit fixtures."""
+    return 1000 + b
+
+
+def _c4_logit_worker(args):
+    """One C4 sequence through the restatement, one forward at a time, keeping
+    the logit rows at C4_LOGIT_STEPS. Greedy sequences are fed the stored
+    golden ids (and each argmax is checked against them); sampled sequences
+    draw with src/sim_sample.cc's full-vocabulary walk (top_k 0) from
+    c4_seed(b), the seed rule of src/llama_model.cc:111."""
+    index, prompt, golden_ids, sampled = args
+    cfg = syn.SMOLLM2_135M
+    _, dense = syn.llama_int8(cfg, 4)
+    orc = Restated()
+    model = LlamaHandle(orc, cfg)
+    model.load(dense)
+    t = time.time()
+    steps = cfg["context"] - len(prompt)
+    rows, ids = [], []
+    rng = c4_seed(index)
+    model.forward_ids(prompt, True)
+    for n in range(steps + 1):
+        logits = model.logits()
+        if n in C4_LOGIT_STEPS:
+            rows.append(logits)
+        if n == steps:
+            break
+        if sampled:
+            nxt, rng = orc.sample(logits, cfg["vocab"], C4_TEMPERATURE, rng, 0)
+        else:
+            nxt = int(golden_ids[n])
+            assert int(np.argmax(logits)) == nxt, (index, n)
+        ids.append(nxt)
+        model.forward_ids(np.array([nxt], np.int32), False)
+    model.close()
+    head = None
+    if sampled:
+        # Pin the loop above against the reference's own Generate.
+        mr = LlamaHandle(Reference(), cfg)
+        mr.load(dense)
+        head = mr.generate(prompt, 8, temperature=C4_TEMPERATURE, seed=c4_seed(index))
+        mr.close()
+        assert np.array_equal(head, np.array(ids[:8], np.int32)), (index, head, ids[:8])
+    print(f"c4 logits seq {index} ({'sampled' if sampled else 'greedy'}): {time.time() - t:.0f}s", flush=True)
+    return index, sampled, np.array(ids, np.int32), np.stack(rows)
+
+
+def make_c4_logits(workers):
+    """C4 logit rows of two greedy and two sampled sequences at the decode
+    depths C4_LOGIT_STEPS, plus the sampled sequences' ids."""
+    cfg = syn.SMOLLM2_135M
+    prompts = syn.prompts(cfg, 32, 512, 41)
+    golden = np.load(HERE / "c4_ids.npz")["ids"]
+    jobs = [(b, prompts[b], golden[b], False) for b in C4_GREEDY_SEQS]
+    jobs += [(b, prompts[b], None, True) for b in C4_SAMPLED_SEQS]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(min(workers, len(jobs))) as pool:
+        results = pool.map(_c4_logit_worker, jobs)
+    out = {"steps": np.array(C4_LOGIT_STEPS, np.int32), "temperature": np.float32(C4_TEMPERATURE)}
+    greedy = [r for r in results if not r[1]]
+    sampled = [r for r in results if r[1]]
+    out["greedy_seqs"] = np.array([r[0] for r in greedy], np.int32)
+    out["greedy_logits"] = np.stack([r[3] for r in greedy])  # [seq, step, vocab]
+    out["sampled_seqs"] = np.array([r[0] for r in sampled], np.int32)
+    out["sampled_seeds"] = np.array([c4_seed(r[0]) for r in sampled], np.uint32)
+    out["sampled_ids"] = np.stack([r[2] for r in sampled])
+    out["sampled_logits"] = np.stack([r[3] for r in sampled])
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--c4", action="store_true")
+    ap.add_argument("--c4-logits", action="store_true")
     ap.add_argument("--workers", type=int, default=8)
     args = ap.parse_args()
+    if args.c4_logits:
+        np.savez_compressed(HERE / "c4_logits.npz", **make_c4_logits(args.workers))
+        return
     ref, orc = Reference(), Restated()
     if args.c4:
         np.savez_compressed(HERE / "c4_ids.npz", **make_c4(ref, orc, args.workers))

@@ -36,7 +36,14 @@ def tables(ctx, hd, theta=10000.0):
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 
+# C4's decode launch: 32 sequences, 3 kv heads, contexts 512..2048 (the
+# kernel splits each (sequence, kv head) over a 4-CTA cluster at this size).
+C4_POS = [511, 2047, 1023, 1024, 1279, 1280, 2046, 600, 1900, 767, 1535, 1536, 2000, 513, 1111, 1999,
+          640, 704, 1088, 1152, 1408, 1471, 1664, 1727, 1791, 1855, 1920, 1983, 2010, 2040, -1, 1300]
+
+
 @pytest.mark.parametrize("heads,kvh,ctx,pos", [
+    (9, 3, 2048, C4_POS),
     (9, 3, 1300, [0, 63, 64, 700, 1299, -1, 127, 1000]),
     (4, 4, 200, [5, 199, -1, 64]),
     (8, 1, 520, [511, 512, 0]),

@@ -145,7 +145,17 @@ def test_c3_ids_logits_counters(c3):
     assert c3.bytes_to_device() == 16 and c3.bytes_to_host() == 64 * 4
 
 
-def test_c4_batched_ids(lib, cuda):
+@pytest.fixture(scope="module")
+def c4_model(lib, cuda):
+    cfg = syn.SMOLLM2_135M
+    planes, dense = syn.llama_int8(cfg, 4)
+    model = Llama(cfg)
+    model.load_int8(planes, dense)
+    yield model
+    model.close()
+
+
+def test_c4_batched_ids(c4_model):
     """C4: 32 x 512-token prompts decoded greedily to 2048 context on the int8
     model, every id against the reference's (tests/golden/c4_ids.npz)."""
     path = GOLDEN / "c4_ids.npz"
@@ -153,12 +163,8 @@ def test_c4_batched_ids(lib, cuda):
         pytest.skip("c4_ids.npz has not been generated")
     g = np.load(path)
     cfg = syn.SMOLLM2_135M
-    planes, dense = syn.llama_int8(cfg, 4)
-    model = Llama(cfg)
-    model.load_int8(planes, dense)
     prompts = syn.prompts(cfg, 32, 512, 41)
-    out = model.generate_batch(list(prompts), cfg["context"] - 512)
-    model.close()
+    out = c4_model.generate_batch(list(prompts), cfg["context"] - 512)
     got = np.stack(out)
     want = g["ids"]
     assert got.shape == want.shape
@@ -168,3 +174,51 @@ def test_c4_batched_ids(lib, cuda):
         step = int(np.argmax(got[b] != want[b]))
         detail.append((b, step, float(g["gaps"][b, step])))
     assert not diverged, f"sequences diverged (seq, step, reference top-2 gap): {detail}"
+
+
+def _c4_golden():
+    path = GOLDEN / "c4_logits.npz"
+    if not path.is_file():
+        pytest.skip("c4_logits.npz has not been generated")
+    return np.load(path)
+
+
+def test_c4_logits_greedy(c4_model):
+    """C4 logit rows through generate_batch's captured decode loop (32
+    sequences, int8 weights), against the reference's rows
+    (tests/golden/c4_logits.npz) at rtol = atol = 1e-4: after the 512-token
+    prefill, and after 513 and 1536 decode forwards (positions 1024 and 2047,
+    the last row of the context)."""
+    g = _c4_golden()
+    cfg = syn.SMOLLM2_135M
+    prompts = list(syn.prompts(cfg, 32, 512, 41))
+    want_ids = np.load(GOLDEN / "c4_ids.npz")["ids"]
+    for j, n in enumerate(g["steps"]):
+        ids = c4_model.generate_batch(prompts, int(n))
+        rows = c4_model.logits(32)
+        for i, b in enumerate(g["greedy_seqs"]):
+            assert np.array_equal(ids[b], want_ids[b, :n])
+            want = g["greedy_logits"][i, j]
+            np.testing.assert_allclose(rows[b], want, rtol=TOL, atol=TOL, err_msg=f"seq {b} after {n} forwards")
+            if b == 0:  # the reference's own check, on the device (src/llama_model.cc:572-587)
+                assert c4_model.logit_max_abs(want) <= TOL
+
+
+def test_c4_logits_sampled(c4_model):
+    """The same rows on full-vocabulary sampled sequences (temperature 1,
+    top_k 0, one seed per sequence): the drawn ids equal the reference's and
+    the contexts are made of diverse ids, not a greedy repeat loop."""
+    g = _c4_golden()
+    cfg = syn.SMOLLM2_135M
+    prompts = list(syn.prompts(cfg, 32, 512, 41))
+    seeds = 1000 + np.arange(32, dtype=np.uint32)
+    assert np.array_equal(seeds[g["sampled_seqs"]], g["sampled_seeds"])
+    for i in range(len(g["sampled_seqs"])):
+        assert len(np.unique(g["sampled_ids"][i])) > 1000  # the context is not a repeat loop
+    for j, n in enumerate(g["steps"]):
+        ids = c4_model.generate_batch(prompts, int(n), temperature=float(g["temperature"]), seeds=seeds, top_k=0)
+        rows = c4_model.logits(32)
+        for i, b in enumerate(g["sampled_seqs"]):
+            assert np.array_equal(ids[b], g["sampled_ids"][i, :n]), f"seq {b}: drawn ids differ"
+            np.testing.assert_allclose(rows[b], g["sampled_logits"][i, j], rtol=TOL, atol=TOL,
+                                       err_msg=f"seq {b} after {n} forwards")

@@ -66,3 +66,24 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(lib, cuda):
                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 1
     assert "4 MiB" in lib.accel_b200_last_error().decode()
+
+
+@pytest.mark.parametrize("batch,heads,kvh,max_len,chunk", [
+    (1 << 20, 0, 8, 64, 64),   # no heads: the workspace size reads 0, the call must still be rejected
+    (4, 9, 3, 64, 0),          # chunk 0
+    (4, 3, 9, 64, 64),         # more kv heads than heads
+    (4, 9, -3, 64, 64),        # negative kv heads
+    (16385, 1, 1, 1, 64),      # more (sequence, kv head) pairs than arrival counters
+    (-1, 9, 3, 64, 64),        # negative batch
+])
+def test_noalloc_rejects_bad_arguments_before_queueing(lib, cuda, batch, heads, kvh, max_len, chunk):
+    """Bad arguments return the error code without touching the scratch: the
+    stream stays usable and a correct call afterwards still matches."""
+    buf = torch.zeros(64 * 64, dtype=torch.float32, device="cuda")
+    lens = torch.ones(8, dtype=torch.int32, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = lib.accel_b200_attention_decode_noalloc(_p(buf), 0, _p(buf), _p(buf), 64, 64, 64, _p(lens), batch, heads,
+                                                 kvh, 64, max_len, chunk, _p(buf), 0, None, stream)
+    assert rc == 1
+    torch.cuda.synchronize()
+    assert not buf.any()  # nothing was written
