@@ -11,7 +11,8 @@ sequences (weak scaling, no data-path collective).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 Prints one JSON line. `--impl reference` times the AccelEP reference's own
-CPU path (oracle/_ref, compiled from its sources) on the host cores.
+CPU path (oracle/_ref, compiled from its sources) on the host cores, on a
+sample of the same C4 job extrapolated to the whole job.
 """
 
 import argparse
@@ -121,36 +122,100 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- CPU baseline
+#
+# The reference (oracle/_ref/libaccel_ref_c4.so: AccelEP's own src/llama_model.cc
+# on SimDevice, single-threaded) takes minutes per C4 sequence, so both CPU legs
+# time a sample of C4's real work and extrapolate to the whole job:
+#   - the 512-token prefill as 16 chunks of 32 prompt rows, each a reference
+#     forward at its own position over the rows before it (the chunks sum to
+#     0.96 of one 512-row forward on the same core: the estimate favours the
+#     reference slightly);
+#   - the 1536 decode steps as 16 bins of 96 positions over [512, 2048); in
+#     each bin WINDOW consecutive reference decode forwards are timed at the
+#     bin's middle, the model placed at that context length first
+#     (ref_llama_fill_context), so attention runs over the real number of rows.
+# Whole-job time of one sequence = sum of chunk times + sum over bins of 96 x
+# the bin's mean step time. P concurrent processes (P = min(host cores, 32),
+# one sequence each, as the reference would serve 32 sequences on P cores)
+# finish 32 sequences in ceil(32 / P) such times.
 
-def _cpu_worker(args):
-    """One single-threaded reference process: the C4 model (dequantized int8
-    weights, which is the reference's int8 arithmetic) generating `new` ids
-    after a short prompt. Returns (ids, seconds)."""
-    index, prompt_len, new = args
+PREFILL_CHUNK = 32
+DECODE_BINS = 16
+BIN_WIDTH = NEW // DECODE_BINS
+WINDOW = 4
+_REF = {}
+
+
+def _ref_init():
+    """Pool initializer: one reference model per process, loaded once."""
     sys.path.insert(0, str(ROOT))
-    from oracle.oracle import LlamaHandle, Reference
+    from oracle.oracle import LlamaHandle, ReferenceLlamaTiming
 
-    cfg = dict(syn.SMOLLM2_135M, context=prompt_len + new + 1)
+    cfg = syn.SMOLLM2_135M
     _, dense = syn.llama_int8(cfg, WEIGHT_SEED)
-    model = LlamaHandle(Reference(), cfg)
+    model = LlamaHandle(ReferenceLlamaTiming(), cfg)
     model.load(dense)
-    del dense
-    prompt = syn.prompts(syn.SMOLLM2_135M, SEQS, PROMPT, PROMPT_SEED)[index % SEQS][:prompt_len]
-    t0 = time.perf_counter()
-    ids = model.generate(prompt, new)
-    return len(ids), time.perf_counter() - t0
+    _REF["model"] = model
+    _REF["prompts"] = syn.prompts(cfg, SEQS, PROMPT, PROMPT_SEED)
 
 
-def reference_throughput(workers, prompt_len=8, new=24):
-    """Aggregate decode tok/s of `workers` reference processes running at once."""
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(workers) as pool:
+def _ref_task(task):
+    """("prefill", chunk, seq) or ("decode", bin, seq) -> (kind, index, seconds
+    per chunk or per decode step)."""
+    kind, index, seq = task
+    model, prompt = _REF["model"], _REF["prompts"][seq % SEQS]
+    if kind == "prefill":
+        first = index * PREFILL_CHUNK
+        model.fill_context(first, seq + 1)
         t0 = time.perf_counter()
-        results = pool.map(_cpu_worker, [(i, prompt_len, new) for i in range(workers)])
-        wall = time.perf_counter() - t0
-    tokens = sum(r[0] for r in results)
-    per_proc = max(r[1] for r in results)
-    return tokens / per_proc, tokens, per_proc, wall
+        model.forward_ids(prompt[first:first + PREFILL_CHUNK], False)
+        return kind, index, time.perf_counter() - t0
+    pos = PROMPT + index * BIN_WIDTH + (BIN_WIDTH - WINDOW) // 2
+    model.fill_context(pos, seq + 1)
+    t0 = time.perf_counter()
+    for i in range(WINDOW):
+        model.forward_ids(prompt[i:i + 1], False)
+    return kind, index, (time.perf_counter() - t0) / WINDOW
+
+
+def _job_seconds(results):
+    """One sequence's whole C4 job from the sampled chunk and step times
+    (several samples of one chunk or bin are averaged)."""
+    chunks, bins = {}, {}
+    for kind, index, sec in results:
+        (chunks if kind == "prefill" else bins).setdefault(index, []).append(sec)
+    prefill = sum(statistics.mean(chunks[i]) for i in range(PROMPT // PREFILL_CHUNK))
+    decode = sum(BIN_WIDTH * statistics.mean(bins[i]) for i in range(DECODE_BINS))
+    return prefill, decode
+
+
+def c4_tasks():
+    return ([("prefill", i, i) for i in range(PROMPT // PREFILL_CHUNK)] +
+            [("decode", i, i) for i in range(DECODE_BINS)])
+
+
+class ReferencePool:
+    """`procs` single-threaded reference processes, each holding the C4 model
+    (the reference fp32 Llama with the dequantized int8 weights, which is the
+    reference's int8 arithmetic)."""
+
+    def __init__(self, procs):
+        self.procs = procs
+        self.pool = mp.get_context("spawn").Pool(procs, initializer=_ref_init)
+
+    def step(self):
+        """One sample of C4 (all 16 chunks and 16 bins, spread over the
+        processes, which run concurrently). Returns (tok/s, job seconds per
+        sequence, prefill seconds, decode seconds)."""
+        results = self.pool.map(_ref_task, c4_tasks(), chunksize=1)
+        prefill, decode = _job_seconds(results)
+        job = prefill + decode
+        rounds = -(-SEQS // self.procs)
+        return SEQS * NEW / (rounds * job), job, prefill, decode
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
 
 
 def run_reference(args):
@@ -158,26 +223,56 @@ def run_reference(args):
     if rank != 0:
         return
     cores = os.cpu_count() or 1
-    workers = max(1, min(SEQS, cores))
-    sample = (f"{workers} concurrent single-threaded reference processes (oracle/_ref, compiled from the AccelEP "
-              f"sources), each generating 24 greedy ids after an 8-token prompt on the C4 model (dequantized int8 "
-              f"weights); tok/s = all ids / slowest process time")
+    procs = max(1, min(SEQS, cores))
+    pool = ReferencePool(procs)
     for _ in range(args.warmup):
-        reference_throughput(workers)
-    vals = []
+        pool.step()
+    vals, jobs = [], []
     t_all = time.perf_counter()
     for _ in range(args.steps):
-        v, _, _, _ = reference_throughput(workers)
+        v, job, prefill, decode = pool.step()
         vals.append(v)
+        jobs.append((job, prefill, decode))
     elapsed = time.perf_counter() - t_all
+    pool.close()
     value = statistics.median(vals)
+    job, prefill, decode = jobs[vals.index(value)] if value in vals else jobs[0]
+    sample = (f"C4 extrapolated from a sample of its real work, run on {procs} concurrent single-threaded reference "
+              f"processes (oracle/_ref/libaccel_ref_c4.so: AccelEP's src/llama_model.cc on SimDevice, the C4 model "
+              f"with dequantized int8 weights): the 512-token prefill as 16 timed 32-row chunks and the 1536 decode "
+              f"steps as 16 bins of 96 positions over contexts 512..2047 with {WINDOW} timed steps at each bin's "
+              f"middle; one sequence's job = {job:.0f} s (prefill {prefill:.0f} s, decode {decode:.0f} s); 32 "
+              f"sequences on {procs} processes = {-(-SEQS // procs)} x that; median of {args.steps} samples")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / max(1, args.steps),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (int8 weights dequantized)",
             "data": "synthetic", "config": config(args.gpus),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": "reference", "sample": sample,
+                             "extrapolated": True, "job_seconds_per_seq": job},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_one_core():
+    """bench.py's cpu_baseline leg (rank 0, N = 1): the same C4 sample on one
+    reference process, 4 of the 16 chunks and 4 of the 16 bins, with the step
+    time linear in the context (least squares over the 4 bins) and the chunks'
+    mean for the other chunks. About 15 s of CPU work after the model loads."""
+    pool = ReferencePool(1)
+    tasks = [("prefill", i, i) for i in (0, 5, 10, 15)] + [("decode", i, i) for i in (1, 5, 10, 14)]
+    results = pool.pool.map(_ref_task, tasks, chunksize=1)
+    pool.close()
+    chunk = statistics.mean(sec for kind, _, sec in results if kind == "prefill")
+    pts = [(PROMPT + i * BIN_WIDTH + BIN_WIDTH // 2, sec) for kind, i, sec in results if kind == "decode"]
+    slope, icpt = np.polyfit([p for p, _ in pts], [t for _, t in pts], 1)
+    decode = sum(icpt + slope * p for p in range(PROMPT, CONTEXT))
+    job = (PROMPT // PREFILL_CHUNK) * chunk + decode
+    return {"value": NEW / job, "unit": UNIT, "cores": 1, "kind": "reference", "extrapolated": True,
+            "job_seconds_per_seq": job,
+            "sample": f"one single-threaded reference process (oracle/_ref/libaccel_ref_c4.so, AccelEP's "
+                      f"src/llama_model.cc) on C4: 4 of the 16 32-row prefill chunks and {WINDOW} decode steps at each "
+                      f"of contexts {', '.join(str(p) for p, _ in pts)}, extrapolated (chunk mean x 16; step time "
+                      f"linear in the context, summed over 512..2047) to one sequence's whole job of {job:.0f} s"}
 
 
 # ------------------------------------------------------------------ B200 arm
@@ -409,11 +504,7 @@ def run_b200(args):
         gemv = gemv_roofline(torch)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cores = 1
-            v, toks, per, _ = reference_throughput(1, prompt_len=8, new=48)
-            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "reference",
-                   "sample": f"one single-threaded reference process (oracle/_ref), {toks} greedy ids after an "
-                             f"8-token prompt on the C4 model (dequantized int8 weights) in {per:.1f} s"}
+            cpu = cpu_baseline_one_core()
         cfg_line = config(world)
         if prompt_len != PROMPT or new != NEW:
             cfg_line["workload"] = f"profiling variant: prompt {prompt_len}, {new} new ids (not the C4 bench number)"

@@ -17,6 +17,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libaccel_ref.so"
+REF_C4_LIB = HERE / "_ref" / "libaccel_ref_c4.so"
 # The AccelEP checkout the reference library is built from: ACCEL_REF_ROOT,
 # else a directory named `reference` beside this repository's root.
 REF_SOURCES = Path(os.environ.get("ACCEL_REF_ROOT", str(HERE.parent.parent / "reference")))
@@ -235,6 +236,7 @@ class Reference(_Common):
     """The AccelEP reference compiled from source (oracle/_ref)."""
 
     prefix = "ref_"
+    llama_api = True  # LlamaHandle drives the reference's own accel_llama_* API
 
     def __init__(self, path=REF_LIB):
         if not Path(path).is_file():
@@ -308,6 +310,27 @@ class Reference(_Common):
         return dict(zip(keys, (int(v) for v in out)))
 
 
+class ReferenceLlamaTiming:
+    """The reference's Llama alone (oracle/_ref/libaccel_ref_c4.so: its
+    src/llama_model.cc unmodified, plus ref_llama_fill_context, which places a
+    model at a given context length without running the forwards that would
+    fill it). bench.py times the reference's decode deep into the context
+    with it; nothing checks values through it."""
+
+    llama_api = True
+
+    def __init__(self, path=REF_C4_LIB):
+        if not Path(path).is_file():
+            if REF_SOURCES.is_dir():
+                build()
+            if not Path(path).is_file():
+                raise FileNotFoundError(f"{path} is not built")
+        self.lib = ctypes.CDLL(str(path))
+        _bind_llama_api(self.lib)
+        self.lib.ref_llama_fill_context.restype = ctypes.c_int
+        self.lib.ref_llama_fill_context.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_uint32]
+
+
 class LlamaConfig(ctypes.Structure):
     """AccelLlamaConfig (include/accel/sim_api.h:44-54)."""
 
@@ -344,7 +367,7 @@ class LlamaHandle:
         self.owner = owner
         self.cfg = cfg
         self.lib = owner.lib
-        self.ref = isinstance(owner, Reference)
+        self.ref = getattr(owner, "llama_api", False)
         if self.ref:
             c = LlamaConfig(cfg["vocab"], cfg["hidden"], cfg["layers"], cfg["heads"], cfg["kv_heads"],
                             cfg["intermediate"], cfg["context"], cfg["eps"], cfg["rope_theta"])
@@ -384,6 +407,11 @@ class LlamaHandle:
         fn = self.lib.accel_llama_forward_ids if self.ref else self.lib.orc_llama_forward_ids
         if fn(self.h, _p(ids, _i32p), ids.size, 1 if reset else 0) != 0:
             raise RuntimeError("forward rejected")
+
+    def fill_context(self, rows, seed=1):
+        """ReferenceLlamaTiming only: the model's cache holds `rows` rows."""
+        if self.lib.ref_llama_fill_context(self.h, rows, seed) != 0:
+            raise RuntimeError(self.lib.accel_llama_last_error().decode())
 
     def logits(self):
         if self.ref:
