@@ -90,6 +90,21 @@ void CheckCuda(cudaError_t err, const char* what) {
   if (err != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(err));
 }
 
+// The counters SimDevice keeps (src/sim_device.cc:171-208): the host
+// project's own (src/runtime.cc:450-458) when this file is built inside it,
+// this library's otherwise.
+#ifdef ACCEL_B200_USE_HOST_CONTRACT
+void CountKernelMatmul() { accel::NoteKernelMatmul(); }
+void CountTranspose() { accel::NoteDeviceTranspose(); }
+void CountToDevice(size_t bytes) { accel::NoteBytesToDevice(bytes); }
+void CountToHost(size_t bytes) { accel::NoteBytesToHost(bytes); }
+#else
+void CountKernelMatmul() { NoteKernelMatmuls(1); }
+void CountTranspose() {}
+void CountToDevice(size_t bytes) { NoteBytesToDevice(bytes); }
+void CountToHost(size_t bytes) { NoteBytesToHost(bytes); }
+#endif
+
 int32_t ActCode(accel::Activation act) {
   return act == accel::Activation::Relu ? ACCEL_B200_ACT_RELU
          : act == accel::Activation::Gelu ? ACCEL_B200_ACT_GELU
@@ -171,7 +186,7 @@ class B200Device final : public accel::Device {
     if (src == nullptr || dst.data == nullptr || bytes > dst.bytes) throw std::invalid_argument("invalid host-to-device copy");
     DeviceScope scope(ordinal_);
     CheckCuda(cudaMemcpyAsync(dst.data, src, bytes, cudaMemcpyHostToDevice, stream_), "host-to-device copy");
-    NoteBytesToDevice(bytes);
+    CountToDevice(bytes);
   }
 
   void CopyDeviceToHost(void* dst, accel::DeviceBuffer src, size_t bytes) override {
@@ -180,7 +195,7 @@ class B200Device final : public accel::Device {
     DeviceScope scope(ordinal_);
     CheckCuda(cudaMemcpyAsync(dst, src.data, bytes, cudaMemcpyDeviceToHost, stream_), "device-to-host copy");
     CheckCuda(cudaStreamSynchronize(stream_), "device-to-host copy");
-    NoteBytesToHost(bytes);
+    CountToHost(bytes);
   }
 
   void MatMul(accel::DeviceBuffer a, accel::DeviceBuffer b, accel::DeviceBuffer c, int64_t m, int64_t k,
@@ -191,7 +206,7 @@ class B200Device final : public accel::Device {
     DeviceScope scope(ordinal_);
     Check(accel_b200_matmul(static_cast<const float*>(a.data), static_cast<const float*>(b.data),
                             static_cast<float*>(c.data), m, k, n, stream_));
-    NoteKernelMatmuls(1);
+    CountKernelMatmul();
   }
 
   void Transpose(accel::DeviceBuffer src, accel::DeviceBuffer dst, int64_t rows, int64_t cols) override {
@@ -199,6 +214,7 @@ class B200Device final : public accel::Device {
     RequireBytes(dst, CheckedBytes(cols, rows), "Transpose destination is out of range");
     DeviceScope scope(ordinal_);
     Check(accel_b200_transpose(static_cast<const float*>(src.data), static_cast<float*>(dst.data), rows, cols, stream_));
+    CountTranspose();
   }
 
   void GemmEpilogue(accel::DeviceBuffer c, int64_t m, int64_t n, float alpha, const accel::DeviceBuffer* bias,
@@ -336,7 +352,7 @@ class B200Device final : public accel::Device {
     void* ws = Workspace(need);
     Check(accel_b200_matmul_q8(static_cast<const float*>(a.data), k, &plane, static_cast<float*>(c.data), n, m, k, n,
                                nullptr, ws, need, stream_));
-    NoteKernelMatmuls(1);
+    CountKernelMatmul();
   }
 
  private:

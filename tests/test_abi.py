@@ -92,3 +92,23 @@ def test_synthetic_is_deterministic():
     x, w, sc = syn.int8_gemm(4, 8, 16, 1)
     assert w.min() >= -127 and w.max() <= 127 and sc.min() >= 1e-3 and sc.max() <= 1e-2
     assert np.array_equal(syn.prompts(syn.SMOLLM2_135M, 2, 5, 1), syn.prompts(syn.SMOLLM2_135M, 2, 5, 1))
+
+
+def test_dropin_libraries_export_the_reference_entry_points():
+    """tests/dropin builds the reference's own runtime, Llama and one-matmul
+    API on B200Device (libaccel_dropin.so) and the plugin on it
+    (libaccel_ep_b200.so); both load without a GPU and export what their
+    callers bind (src/ep.cc:1985-2022 for the plugin)."""
+    import pytest
+
+    base = ROOT / "tests" / "_build" / "dropin"
+    if not (base / "libaccel_dropin.so").is_file():
+        pytest.skip("the drop-in build needs the AccelEP sources (make -C tests/dropin)")
+    dropin = ctypes.CDLL(str(base / "libaccel_dropin.so"))
+    for name in ("accel_llama_create", "accel_llama_generate", "accel_llama_forward_ids", "accel_sim_matmul",
+                 "dropin_execute_matmul_q", "dropin_mlp_block", "dropin_device_name"):
+        assert hasattr(dropin, name), name
+    if (base / "libaccel_ep_b200.so").is_file():
+        ep = ctypes.CDLL(str(base / "libaccel_ep_b200.so"))
+        for name in ("CreateEpFactories", "ReleaseEpFactory", "AccelEpKernelMatmuls", "AccelEpBytesToDevice"):
+            assert hasattr(ep, name), name
