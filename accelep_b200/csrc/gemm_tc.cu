@@ -135,6 +135,7 @@ struct TcArgs {
   int32_t* status;
   int32_t vec_store;   // c and ldc allow 16-byte row stores
   int32_t silu_pairs;  // gate|up columns in 64-column pairs; C = SiluMul(gate, up), n / 2 columns
+  int32_t res_vec;     // the epilogue's residual allows 16-byte row loads
   Epilogue ep;
   PeerOut peers;  // copies of C on other GPUs (n = 0: none)
 };
@@ -299,12 +300,15 @@ __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int6
 
 // In-kernel operand: the fp32 tiles of the CTA's k blocks (block b at
 // ytiles + b * tiles * R * 128 floats: A, then up for SiluMul; rows of 128 k;
-// rows past the matrix and k past K read as zero) are formed as the mode does
-// (in place), the exponents over the range found (exp_s, every row of the
-// tile), and the digit planes of block b written into stage b: plane p, row r
-// at (p R + r) * 128, the 16-byte chunk j of a row stored at j ^ (r % 8) (the
-// TMA's 128-byte swizzle). Converter warp w takes block w % nkb, rows w / nkb,
-// + CW / nkb, ...; lane l the quad k = 4l .. 4l + 3 of the block.
+// rows past the matrix and k past K read as zero) are formed as the mode does,
+// the exponents over the range found (exp_s, every row of the tile), and the
+// digit planes of block b written into stage b: plane p, row r at (p R + r) *
+// 128, the 16-byte chunk j of a row stored at j ^ (r % 8) (the TMA's 128-byte
+// swizzle). Converter warp w takes block w % nkb, rows w / nkb, + CW / nkb,
+// ...; lane l the quad k = 4l .. 4l + 3 of the block. Tiles of up to 32 rows
+// keep a warp's formed rows in registers between the maxima and the digits
+// (all of a warp's shared-memory loads issue back to back); 64-row tiles
+// write the formed rows back in place and read them again.
 template <int R, int M, int CW>
 __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0, const double* inv, float* ytiles,
                                             uint32_t* amax, int32_t* exp_s, uint8_t* stages, int stage_bytes,
@@ -318,42 +322,77 @@ __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0
   if constexpr (M == kANorm) {
     if (k0 + b * kBk + kb < g.k) gam = __ldg(reinterpret_cast<const float4*>(g.gamma + k0 + b * kBk + kb));
   }
-#pragma unroll 4
-  for (int r = r0; r < R; r += rstep) {
-    float4* at = reinterpret_cast<float4*>(y_at + r * kBk);
-    const float4 v = *at;
-    float4 y = v;
+  const auto form = [&](float4 v, int r) {
     if constexpr (M == kASilu) {
       const float4 u = *reinterpret_cast<const float4*>(y_at + R * kBk + r * kBk);
-      y = make_float4(SiluMul(v.x, u.x), SiluMul(v.y, u.y), SiluMul(v.z, u.z), SiluMul(v.w, u.w));
-      *at = y;
+      return make_float4(SiluMul(v.x, u.x), SiluMul(v.y, u.y), SiluMul(v.z, u.z), SiluMul(v.w, u.w));
     } else if constexpr (M == kANorm) {
       const double iv = inv[r];
-      y = make_float4(__fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), gam.x),
-                      __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), gam.y),
-                      __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), gam.z),
-                      __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), gam.w));
-      *at = y;
+      return make_float4(__fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), gam.x),
+                         __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), gam.y),
+                         __fmul_rn(static_cast<float>(static_cast<double>(v.z) * iv), gam.z),
+                         __fmul_rn(static_cast<float>(static_cast<double>(v.w) * iv), gam.w));
+    } else {
+      return v;
     }
-    const uint32_t m = __reduce_max_sync(kFull, AbsMaxBits(y));
-    if (lane == 0) amax[2 * r + b] = m;
-  }
-  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");  // converter warps only
+  };
   const auto row_exponent = [&](int r) {
     return RowExponent(nkb > 1 ? max(amax[2 * r], amax[2 * r + 1]) : amax[2 * r]);
   };
-  if (ct < R) exp_s[ct] = row_exponent(ct);
   uint8_t* xs = stages + b * stage_bytes;
   const int chunk = kb >> 4, byte = kb & 15;
-#pragma unroll 4
-  for (int r = r0; r < R; r += rstep) {
-    const int32_t e = row_exponent(r);
-    const float4 y = *reinterpret_cast<const float4*>(y_at + r * kBk);
+  const auto store_digits = [&](float4 y, int r, int32_t e) {
     uint32_t d[kDigits] = {0u, 0u, 0u, 0u};
     if (e != kBadRow) FourDigits(y, FixScale(e), d);
     const int off = (((chunk ^ (r & 7)) << 4) | byte) + r * kBk;
 #pragma unroll
     for (int p = 0; p < kDigits; ++p) *reinterpret_cast<uint32_t*>(xs + p * R * kBk + off) = d[p];
+  };
+  if constexpr (R <= 32) {
+    // At most R * 2 / CW rows per warp (nkb <= 2); r is the same for the
+    // whole warp, so the shuffles below see every lane.
+    constexpr int kRows = (R * kInKernelBlocks + CW - 1) / CW;
+    float4 y[kRows];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int r = r0 + i * rstep;
+      y[i] = r < R ? *reinterpret_cast<const float4*>(y_at + r * kBk) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int r = r0 + i * rstep;
+      if (r < R) y[i] = form(y[i], r);
+    }
+    uint32_t m[kRows];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) m[i] = __reduce_max_sync(kFull, AbsMaxBits(y[i]));
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        const int r = r0 + i * rstep;
+        if (r < R) amax[2 * r + b] = m[i];
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");  // converter warps only
+    if (ct < R) exp_s[ct] = row_exponent(ct);
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int r = r0 + i * rstep;
+      if (r < R) store_digits(y[i], r, row_exponent(r));
+    }
+  } else {
+#pragma unroll 4
+    for (int r = r0; r < R; r += rstep) {
+      float4* at = reinterpret_cast<float4*>(y_at + r * kBk);
+      const float4 y = form(*at, r);
+      if constexpr (M != kAF32) *at = y;
+      const uint32_t m = __reduce_max_sync(kFull, AbsMaxBits(y));
+      if (lane == 0) amax[2 * r + b] = m;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");  // converter warps only
+    if (ct < R) exp_s[ct] = row_exponent(ct);
+#pragma unroll 4
+    for (int r = r0; r < R; r += rstep) store_digits(*reinterpret_cast<const float4*>(y_at + r * kBk), r, row_exponent(r));
   }
 }
 
@@ -387,6 +426,21 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
 
   PdlTrigger();
   if (warp == 1) TmemAlloc(&tmem_s, kCols);
+  // The epilogue's column scales, lane l's four columns 4l .. 4l + 3 of the
+  // tile in every warp. The latency-bound in-kernel modes load them here
+  // (immutable, so before the wait); planes mode, whose long weight streams
+  // want the registers, loads them at the epilogue.
+  constexpr bool kEarly = M != kAPlanes;
+  const int64_t cols = Min64(kBn, g.n - n0);
+  const int c4 = lane * 4;
+  float sc[4];
+  const auto load_scales = [&] {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
+    }
+  };
+  if constexpr (kEarly) load_scales();
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       MbarInit(&full_w[s], 1);
@@ -522,8 +576,26 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
   // tiles in rank order (deterministic) through distributed shared memory.
   const int splits = static_cast<int>(gridDim.y);
   const int64_t rows = Min64(R, g.m - row0);
-  const int64_t cols = Min64(kBn, g.n - n0);
   float* tile = reinterpret_cast<float*>(smem);  // [R][kBn], over the stages
+  // Split K: rank `rank` sums rows [rank * rpr, +rpr) of the tile over the
+  // cluster; a thread owns one group of four columns (lane) in rows tid / 32,
+  // + warps, ... Its residual rows are loaded now, so that their latency
+  // overlaps the accumulator read-out and the cluster reduction.
+  const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
+  const int rpr = (static_cast<int>(rows) + splits - 1) / splits;
+  const int r_begin = rank * rpr + warp;
+  const int r_end = min(static_cast<int>(rows), (rank + 1) * rpr);
+  constexpr int kMaxJ = (R / 2 + kThreads / 32 - 1) / (kThreads / 32);  // rows per thread (splits >= 2)
+  float4 res[kEarly ? kMaxJ : 1];
+  const bool res_pre = kEarly && splits > 1 && g.res_vec && !g.silu_pairs && c4 + 4 <= cols;
+  if (res_pre) {
+#pragma unroll
+    for (int j = 0; j < (kEarly ? kMaxJ : 1); ++j) {
+      const int r = r_begin + j * (kThreads / 32);
+      res[j] = r < r_end ? __ldg(reinterpret_cast<const float4*>(g.ep.residual + (row0 + r) * g.ep.residual_ld + n0 + c4))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   if (warp >= 2) {
     // Thread (quarter, lane) holds feature 32 * quarter + lane: its TMEM lane.
     // Column p * R + r holds digit plane p of row r. With eight converter
@@ -563,16 +635,11 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
   }
   TcFenceBeforeSync();
   __syncthreads();
-  if (warp == 1) TmemDealloc(tmem, kCols);
+  if constexpr (!kEarly) load_scales();
   if (splits == 1) {
+    if (warp == 1) TmemDealloc(tmem, kCols);
     // Warp w takes rows w, w + warps, ...; lane l the columns 4l .. 4l + 3.
     if (cta_ok) {
-      const int c4 = lane * 4;
-      float sc[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
-      }
       if (g.silu_pairs) {
         for (int r = warp; r < rows; r += kThreads / 32) {
           StoreSiluPairs(g.c, g.ldc, g.vec_store, row0 + r, n0, lane,
@@ -633,19 +700,6 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
     }
     return;
   }
-  // Rank `rank` sums rows [rank * rpr, +rpr) of the tile over the cluster; a
-  // thread owns one group of four columns (tid % 32) in rows tid / 32, + 6, ...
-  const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
-  const int rpr = (static_cast<int>(rows) + splits - 1) / splits;
-  const int c4 = (tid & 31) * 4;
-  const int r_begin = rank * rpr + (tid >> 5);
-  const int r_end = min(static_cast<int>(rows), (rank + 1) * rpr);
-  constexpr int kMaxJ = (R / 2 + kThreads / 32 - 1) / (kThreads / 32);  // rows per thread (splits >= 2)
-  float sc[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    sc[j] = (c4 + j < cols) ? (g.scalar_scale ? __ldg(g.scale) : __ldg(g.scale + n0 + c4 + j)) : 0.f;
-  }
   ClusterSync();  // every partial tile of the cluster is complete
   float4 sum[kMaxJ];
   if (c4 < cols) {
@@ -688,8 +742,20 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
         const int64_t row = row0 + r;
         const float v[4] = {sum[j].x, sum[j].y, sum[j].z, sum[j].w};
         float o[4];
+        if (res_pre) {
+          // The residual comes last in the epilogue (ApplyEpilogue's order).
+          Epilogue head = g.ep;
+          head.residual = nullptr;
+          const float4 rj = res[kEarly ? j : 0];
+          const float rv[4] = {rj.x, rj.y, rj.z, rj.w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q);
+          for (int q = 0; q < 4; ++q) {
+            o[q] = __fadd_rn(ApplyEpilogue(head, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q), rv[q]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(v[q], sc[q]), row, n0 + c4 + q);
+        }
         if (g.ep.row_sq != nullptr) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -721,6 +787,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
     }
   }
   if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes
+  if (warp == 1) TmemDealloc(tmem, kCols);  // off the reduction's path: the read-out finished above
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // peers are done with this tile
 }
 
@@ -1026,6 +1093,8 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   g.vec_store = (reinterpret_cast<uintptr_t>(c) % 16 == 0 && ldc % 4 == 0) ? 1 : 0;
   g.silu_pairs = silu_pairs ? 1 : 0;
   g.ep = ep;
+  g.res_vec = (ep.residual != nullptr && reinterpret_cast<uintptr_t>(ep.residual) % 16 == 0 && ep.residual_ld % 4 == 0)
+                  ? 1 : 0;
   g.peers = peers != nullptr ? *peers : PeerOut{};
   for (int i = 0; i < g.peers.n; ++i) {
     if (reinterpret_cast<uintptr_t>(g.peers.c[i]) % 16 != 0) g.vec_store = 0;
