@@ -22,9 +22,22 @@ Two ways to assemble Y:
 
 The local product is a parameter so that the nccl gather logic can run on CPU
 ranks (gloo) with a CPU product in tests.
+
+Failure detection (mode "nccl"): with a `deadline` (seconds), the host waits
+for the all-gather at most that long. A peer that died, left the group or
+stalls before the collective then ends the call with CollectiveFailed after
+at most the deadline, and the layer aborts the group's communicator
+(torch.distributed's abort, ncclCommAbort under NCCL) so that no rank keeps
+an operation in flight on it. The call is then synchronous on the host
+(not for CUDA-graph capture); without a deadline the gather is queued on the
+stream as usual and the process group's own timeout is the bound. The
+reference surfaces such failures as the exception RunKernel turns into
+ORT_EP_FAIL (src/ep.cc:1924-1934): CollectiveFailed is a RuntimeError.
 """
 
 import ctypes
+import threading
+import time
 
 import torch
 import torch.distributed as dist
@@ -45,17 +58,28 @@ def _gpu_product(x, w, scale, out):
     return K.matmul_q8(x, w, scale, out=out)
 
 
+class CollectiveFailed(RuntimeError):
+    """The all-gather did not complete within the layer's deadline (a peer
+    died, left or stalled); the group's communicator has been aborted."""
+
+
 class ShardedQ8Linear:
     """One rank's part of the N-sharded product.
 
     w_shard / scale_shard: this rank's column block (shard_columns). product:
     (x, w, scale, out) -> out, the local product (default: the CUDA kernels).
+    deadline: seconds the host waits for the all-gather (mode "nccl"), or
+    None to queue it on the stream without a host wait.
     """
 
-    def __init__(self, w_shard, scale_shard, group=None, product=None, mode="nccl"):
+    def __init__(self, w_shard, scale_shard, group=None, product=None, mode="nccl", deadline=None):
         if mode not in ("nccl", "fused"):
             raise ValueError("mode is 'nccl' or 'fused'")
+        if deadline is not None and (mode != "nccl" or deadline <= 0):
+            raise ValueError("a deadline needs mode 'nccl' and a positive number of seconds")
         self.mode = mode
+        self.deadline = deadline
+        self.aborted = False
         self.group = group
         initialized = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if initialized else 1
@@ -135,9 +159,53 @@ class ShardedQ8Linear:
         self.product(x, self.w, self.scale, local)
         if self.world == 1:
             return local.clone()
-        dist.all_gather_into_tensor(gathered, local, group=self.group)
+        if self.deadline is None:
+            dist.all_gather_into_tensor(gathered, local, group=self.group)
+        else:
+            self._gather_within_deadline(gathered, local)
         # [world * M, Nr] (rank-major) -> [M, world * Nr]: rank r's block is
         # columns r*Nr .. (r+1)*Nr - 1.
         return gathered.view(self.world, m, self.nr).permute(1, 0, 2).reshape(m, self.world * self.nr)
+
+    def _gather_within_deadline(self, gathered, local):
+        if self.aborted:
+            raise CollectiveFailed("the communicator of this layer's group was aborted by an earlier failure")
+        # The host polls the collective's completion against a monotonic
+        # deadline (every backend's Work answers is_completed; not every one
+        # honours a timeout in wait), spinning for the first millisecond and
+        # then polling every 200 us.
+        start = time.monotonic()
+        end = start + self.deadline
+        try:
+            work = dist.all_gather_into_tensor(gathered, local, group=self.group, async_op=True)
+            while not work.is_completed():
+                now = time.monotonic()
+                if now > end:
+                    raise TimeoutError(f"not complete after {now - start:.3f} s")
+                if now - start > 1e-3:
+                    time.sleep(2e-4)
+            work.wait()  # orders the caller's stream after the collective
+        except Exception as ex:  # the deadline, or the backend's lost-peer error
+            self._abort()
+            raise CollectiveFailed(f"all-gather over {self.world} ranks did not complete within {self.deadline} s "
+                                   f"({type(ex).__name__}: {ex}); the communicator was aborted") from ex
+
+    def _abort(self):
+        """Aborts the group's communicator (ncclCommAbort under NCCL): no
+        operation stays in flight on it and later collectives on it fail. The
+        abort runs on a helper thread that the caller waits for at most one
+        second (a backend may hold its abort until the stalled operation
+        ends); the layer refuses further calls either way."""
+        self.aborted = True
+
+        def abort():
+            try:
+                dist.distributed_c10d._abort_process_group(self.group)
+            except Exception:  # a backend without abort: the group is left to its own timeout
+                pass
+
+        helper = threading.Thread(target=abort, name="accel-b200-abort", daemon=True)
+        helper.start()
+        helper.join(timeout=1.0)
 
     __call__ = forward

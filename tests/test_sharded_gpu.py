@@ -79,3 +79,63 @@ def test_sharded_two_gpus(tmp_path, m, k, n):
         np.testing.assert_allclose(ref, full, rtol=1e-4, atol=1e-3 * (it + 1))
     for rank in range(2):
         assert int(np.load(tmp_path / f"status_{rank}.npy")[0]) == 0
+
+
+def _lost_rank_worker(rank, world, port, deadline, out_dir):
+    """NCCL form of the host-side failure case: rank 1 leaves between calls
+    (its stream drained, nothing in flight); rank 0's next gather, waited for
+    with a deadline, ends with CollectiveFailed and ncclCommAbort."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=30))
+    from accelep_b200 import sharded
+    from accelep_b200 import synthetic as syn
+
+    x, w, s = syn.int8_gemm(4, 512, 256, 3)
+    ws, ss = sharded.shard_columns(torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda(), rank, world)
+    layer = sharded.ShardedQ8Linear(ws, ss, mode="nccl", deadline=deadline)
+    y = layer(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"healthy_{rank}.npy"), y.cpu().numpy())
+    if rank == 1:
+        torch.cuda.synchronize()
+        os._exit(0)
+    time.sleep(1.0)  # rank 1 is gone before this rank's next launch
+    t0 = time.monotonic()
+    try:
+        layer(torch.from_numpy(x).cuda())
+        failed = False
+    except sharded.CollectiveFailed:
+        failed = True
+    np.save(os.path.join(out_dir, "rank0.npy"), np.array([failed, time.monotonic() - t0, layer.aborted]))
+    os._exit(0)
+
+
+def test_nccl_gather_deadline_on_a_lost_rank(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    deadline = 3.0
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_lost_rank_worker, args=(r, 2, port, deadline, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert np.array_equal(np.load(tmp_path / "healthy_0.npy"), np.load(tmp_path / "healthy_1.npy"))
+    failed, elapsed, aborted = np.load(tmp_path / "rank0.npy")
+    assert failed and aborted
+    assert elapsed < deadline + 3.0, elapsed
