@@ -368,6 +368,81 @@ def gemv_roofline(torch, reps=20):
     return row
 
 
+def tensor_peaks(torch, reps=10):
+    """Measured dense tensor peaks of this GPU for the C5 fractions at M >= 128
+    (MEASURED_PEAKS.json has bf16 only): cuBLAS int8 (torch._int_mm, int32
+    accumulate) and TF32 (fp32 matmul with TF32 allowed) on 8192^3, timed with
+    CUDA events. Library GEMMs used only as denominators."""
+    n = 8192
+    a8 = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b8 = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    a32 = torch.randn(n, n, device="cuda")
+    b32 = torch.randn(n, n, device="cuda")
+    out = {}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        for name, fn in (("int8_tops", lambda: torch._int_mm(a8, b8)), ("tf32_tflops", lambda: a32 @ b32)):
+            for _ in range(3):
+                fn()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            start.record()
+            for _ in range(reps):
+                fn()
+            end.record()
+            end.synchronize()
+            out[name] = 2.0 * n ** 3 * reps / (start.elapsed_time(end) / 1e3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    del a8, b8, a32, b32
+    torch.cuda.empty_cache()
+    return out
+
+
+def metric_set(torch, peak_hbm, reps=10):
+    """The rest of BASELINE's metric set on one GPU: the C5 sweep grid
+    (M in {1, 16, 128, 2048} x K = N in {4096, 8192, 16384}, accel_b200_matmul_q8
+    graph-replayed over rotated weight copies larger than L2), C1, the C2 MLP
+    chain and C3 (fp32 SmolLM2-135M shape, 4-token prompt, 64 greedy ids)."""
+    from accelep_b200 import profile_cases as PC
+    from accelep_b200.llama import Llama
+
+    peaks = tensor_peaks(torch)
+    grid = []
+    for m in (1, 16, 128, 2048):
+        for kn in (4096, 8192, 16384):
+            row = PC.gemm_case(f"c5_m{m}_k{kn}", m, kn, kn, reps if m < 2048 else 4)
+            torch.cuda.empty_cache()
+            tops = 8.0 * m * kn * kn / row["us"] / 1e6  # int8 MMA ops: four digit planes per product
+            row["frac_hbm"] = round(row["gbs"] / peak_hbm, 3)
+            row["frac_int8_tensor"] = round(tops / peaks["int8_tops"], 3)
+            grid.append(row)
+    c1 = PC.gemm_case("c1_m64_k576_n1536", 64, 576, 1536, 50)
+    c1["frac_hbm"] = round(c1["gbs"] / peak_hbm, 3)
+    c2 = PC.mlp_case(5)
+    cfg = dict(syn.SMOLLM2_135M, context=128)
+    model = Llama(cfg)
+    model.load_fp32(syn.llama_weights(cfg, 3))
+    prompt = syn.prompts(cfg, 1, 4, 11)[0]
+    stream = torch.cuda.ExternalStream(model.stream())
+    model.generate(prompt, 64)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    ids = model.generate(prompt, 64)
+    end.record(stream)
+    end.synchronize()
+    model.close()
+    sec = start.elapsed_time(end) / 1e3
+    c3_tps = len(ids) / sec
+    weight_bytes = 134_479_872 * 4
+    c3 = {"case": "C3 fp32 SmolLM2-135M shape, 4-token prompt + 64 greedy ids (batch 1)", "tok_s": round(c3_tps, 1),
+          "roofline_tok_s": round(peak_hbm * 1e9 / weight_bytes, 1),
+          "frac_hbm": round(c3_tps * weight_bytes / (peak_hbm * 1e9), 3)}
+    return {"tensor_peaks_measured": {k: round(v, 1) for k, v in peaks.items()}, "c5_grid": grid, "c1": c1,
+            "c2": c2, "c3": c3}
+
+
 def c5_sharded(torch, dist, world, rank, reps=10):
     """C5 sweep points with W N-sharded across the ranks
     (accelep_b200/sharded.py), timed with CUDA events, max over ranks. At N > 1
@@ -502,6 +577,7 @@ def run_b200(args):
         achieved, sec, nbytes = attention_roofline(torch, stream)
         p_achieved, p_sec, p_bytes = products_roofline(torch, stream)
         gemv = gemv_roofline(torch)
+        extras = None if args.no_extras or world > 1 else metric_set(torch, peak)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline_one_core()
@@ -536,7 +612,7 @@ def run_b200(args):
                                        "transpose; fused: peer stores from the product epilogue + peer-memory "
                                        "barrier); max over ranks", "ranks": world, "points": sharded_rows,
                                "clocks": c5_clk},
-                "cpu_baseline": cpu, "clocks": clk}
+                "metric_set": extras, "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:
@@ -551,6 +627,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the C1/C2/C3/C5-grid metric set")
     # Shorter jobs for profiling runs only; a bench number uses the defaults.
     ap.add_argument("--prompt-len", type=int, default=0)
     ap.add_argument("--new-tokens", type=int, default=0)
