@@ -396,9 +396,13 @@ __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0
   }
 }
 
-// R = 16 planes kernels (long weight streams, m <= 16) run three CTAs per SM.
+// Planes-mode kernels run several CTAs per SM (three at R = 16, two above:
+// long weight streams, prefill), which the register budget must allow.
+template <int R, int M>
+constexpr int MinBlocks() { return M != kAPlanes ? 1 : (R == 16 ? 3 : 2); }
+
 template <int R, int kStagesT, int M>
-__global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 3 : 1)
+__global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
     Q8GemmTcKernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
                    const __grid_constant__ CUtensorMap tu, TcArgs g) {
   using L = Tc<R, kStagesT, M>;
@@ -500,7 +504,9 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
       // in griddepcontrol.wait (no issue slots) rather than polling barriers
       // while that kernel still runs on this SM.
       PdlWait();
-      if constexpr (M != kAPlanes) ok &= MbarWait(&xready, 0);
+      // Suspended, not polling: a polling warp would compete for the shared
+      // memory pipe with the converter warps that form the operand meanwhile.
+      if constexpr (M != kAPlanes) ok &= MbarWaitSleep(&xready, 0);
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         ok &= MbarWait(&full_w[s], (i / S) & 1);
@@ -550,13 +556,13 @@ __global__ void __launch_bounds__(Threads<R, M>(), (R == 16 && M == kAPlanes) ? 
         if (ct >= valid && ct < R) inv_s[ct] = 0.0;  // rows past the matrix (their tiles read as zero)
         asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
       }
-      for (int i = 0; i < nkb; ++i) ok &= MbarWait(&full_x[i], 0);
+      for (int i = 0; i < nkb; ++i) ok &= MbarWaitSleep(&full_x[i], 0);
       BuildDigits<R, M, kConvWarps>(g, nkb, static_cast<int64_t>(kb_begin) * kBk, inv_s,
                         reinterpret_cast<float*>(smem + S * L::kStage), amax_s, exp_s, smem, L::kStage, ct);
       FenceProxyAsyncSmem();
       __syncwarp();
       if (lane == 0) MbarArrive(&xready);
-      if (nkb > 0) ok &= MbarWait(&accf, 0);
+      if (nkb > 0) ok &= MbarWaitSleep(&accf, 0);
     }
   }
   // Every thread past this point may read the residual or write the output.
