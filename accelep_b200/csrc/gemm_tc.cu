@@ -72,6 +72,7 @@
 #include "accel_b200.h"
 #include "cluster.cuh"
 #include "common.cuh"
+#include "fixed_point.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
 
@@ -83,9 +84,6 @@ constexpr int kBk = 128;                // k per block: one 128-byte swizzle row
 constexpr int kBn = 128;                // output features per tile (MMA M)
 constexpr int kMmaK = 32;               // k per int8 MMA
 constexpr int kWBytes = kBk * kBn;      // int8 weight block, 16 KiB
-constexpr int kDigits = 4;              // int8 digits per fixed-point activation
-constexpr int kExpMin = -96;            // smallest row exponent: keeps 2^(30 - e) a normal float
-constexpr int32_t kBadRow = 0x7fff;     // exponent of a row holding Inf or NaN
 constexpr int kMaxBlocksPerCta = 1023;  // |w d| <= 2^14, so 1023 * 128 k of them sum below 2^31
 constexpr int kInKernelBlocks = 2;      // k blocks of a CTA that forms its own operand
 // Converter warps: eight where they form the operand (latency-bound decode
@@ -186,45 +184,6 @@ __device__ __forceinline__ void StoreSiluPairs(float* c, int64_t ldc, bool vec, 
       dst[3] = y.w;
     }
   }
-}
-
-// ------------------------------------------------------------ fixed point
-
-// Largest |y| of four values as float bits: unsigned order is magnitude order
-// for non-negative floats, and Inf and NaN order above every finite value.
-__device__ __forceinline__ uint32_t AbsMaxBits(float4 y) {
-  const uint32_t a = __float_as_uint(y.x) & 0x7fffffffu, b = __float_as_uint(y.y) & 0x7fffffffu;
-  const uint32_t c = __float_as_uint(y.z) & 0x7fffffffu, d = __float_as_uint(y.w) & 0x7fffffffu;
-  return max(max(a, b), max(c, d));
-}
-
-// The exponent e of a row whose largest |y| has float bits `amax`: every |y|
-// < 2^e (e >= kExpMin), or kBadRow when the row holds Inf or NaN.
-__device__ __forceinline__ int32_t RowExponent(uint32_t amax) {
-  if (amax >= 0x7f800000u) return kBadRow;
-  const int32_t e = static_cast<int32_t>(amax >> 23) - 126;
-  return e < kExpMin ? kExpMin : e;
-}
-
-// 2^(30 - e) as a float (exact: 30 - e lies in [-98, 126]).
-__device__ __forceinline__ float FixScale(int32_t e) { return __int_as_float((127 + 30 - e) << 23); }
-
-// The digit planes of four consecutive elements: word p holds digit p of the
-// four fixed-point values, byte i for element i. For one value, (X + 0x808080)
-// carries the balanced form's carries into bytes 1 .. 3, so XOR 0x808080 of it
-// holds the digits [d3, d2, d1, d0] in bytes 0 .. 3 (d3 = X mod 256 read as a
-// signed byte); a 4 x 4 byte transpose then gathers each digit's bytes.
-__device__ __forceinline__ void FourDigits(float4 y, float s, uint32_t (&w)[kDigits]) {
-  const auto word = [s](float v) {
-    return (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v, s))) + 0x808080u) ^ 0x808080u;
-  };
-  const uint32_t v0 = word(y.x), v1 = word(y.y), v2 = word(y.z), v3 = word(y.w);
-  const uint32_t t0 = __byte_perm(v0, v1, 0x5140), t1 = __byte_perm(v0, v1, 0x7362);  // bytes 0,1 | 2,3 of v0, v1
-  const uint32_t t2 = __byte_perm(v2, v3, 0x5140), t3 = __byte_perm(v2, v3, 0x7362);
-  w[3] = __byte_perm(t0, t2, 0x5410);
-  w[2] = __byte_perm(t0, t2, 0x7632);
-  w[1] = __byte_perm(t1, t3, 0x5410);
-  w[0] = __byte_perm(t1, t3, 0x7632);
 }
 
 // Element quad q (k = 4q .. 4q + 3) of a row as the mode forms it.
@@ -620,16 +579,8 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
         TmemWaitLoads();
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
-          const int32_t e = exp_s[c0 + j];
-          // The exact sum of the planes in int64 (wide multiply-adds), rounded
-          // once; then the exact scaling by 2^(e - 30) (a normal float for
-          // every exponent a row takes).
-          long long sum = static_cast<long long>(static_cast<int32_t>(d[3][j]));
-          sum += static_cast<long long>(static_cast<int32_t>(d[2][j])) * 256;
-          sum += static_cast<long long>(static_cast<int32_t>(d[1][j])) * 65536;
-          sum += static_cast<long long>(static_cast<int32_t>(d[0][j])) * 16777216;
-          const float t = __ll2float_rn(sum);
-          v[j] = e == kBadRow ? __int_as_float(0x7fc00000) : __fmul_rn(t, __int_as_float((127 - 30 + e) << 23));
+          v[j] = PlanesToFloat(static_cast<int32_t>(d[0][j]), static_cast<int32_t>(d[1][j]),
+                               static_cast<int32_t>(d[2][j]), static_cast<int32_t>(d[3][j]), exp_s[c0 + j]);
         }
       } else {
 #pragma unroll
@@ -678,7 +629,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
               for (int q = 0; q < 4; ++q) {
                 if (c4 + q < cols) {
                   const double dv = static_cast<double>(o[q]);
-                  sq += dv * dv;
+                  sq = fma(dv, dv, sq);  // one fused multiply-add, as every kernel that writes row sums does
                 }
               }
             }
@@ -767,7 +718,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
           for (int q = 0; q < 4; ++q) {
             if (c4 + q < cols) {
               const double dv = static_cast<double>(o[q]);
-              sq += dv * dv;
+              sq = fma(dv, dv, sq);  // one fused multiply-add, as every kernel that writes row sums does
             }
           }
         }

@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kGvThreads) Q8GemvKernel(GemvArgs g) {
         for (int q = 0; q < 4; ++q) {
           if (col + q < g.n) {
             const double dv = static_cast<double>(o[q]);
-            sq += dv * dv;
+            sq = fma(dv, dv, sq);  // one fused multiply-add, as every kernel that writes row sums does
           }
         }
       }
