@@ -404,6 +404,27 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
     }
   };
   if constexpr (kEarly) load_scales();
+  // Split K (a cluster along grid y): rank `rank` sums rows [rank * rpr, +rpr)
+  // of the tile over the cluster. A thread owns one group of four columns
+  // (lane) in rows ew, ew + kEpiWarps, ... of that range, where ew is its
+  // epilogue warp: the converter warps in the in-kernel modes (which load
+  // their residual rows right after the wait, long before the epilogue reads
+  // them), every warp in planes mode.
+  const auto split_rows = [&](int* r_begin, int* r_end) {
+    const int splits = static_cast<int>(gridDim.y);
+    const int rows = static_cast<int>(Min64(R, g.m - row0));
+    const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
+    const int rpr = (rows + splits - 1) / splits;
+    const int ew = kEarly ? warp - 2 : warp;
+    // A warp that takes no epilogue rows (producer, MMA issuer) gets an
+    // empty range: r_begin >= r_end for every row it would step through.
+    *r_begin = ew < 0 ? 0 : rank * rpr + ew;
+    *r_end = ew < 0 ? 0 : min(rows, (rank + 1) * rpr);
+  };
+  constexpr int kEpiWarps = kEarly ? kConvWarps : kThreads / 32;
+  constexpr int kMaxJ = (R / 2 + kEpiWarps - 1) / kEpiWarps;  // rows per thread (splits >= 2)
+  float4 res[kEarly ? kMaxJ : 1];
+  const bool res_pre = kEarly && gridDim.y > 1 && g.res_vec && !g.silu_pairs && c4 + 4 <= cols;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       MbarInit(&full_w[s], 1);
@@ -495,6 +516,19 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
     const int ct = tid - 64;
     const int valid = static_cast<int>(Min64(R, g.m - row0));
     PdlWait();
+    if constexpr (kEarly) {
+      if (res_pre) {
+        int r_begin, r_end;
+        split_rows(&r_begin, &r_end);
+#pragma unroll
+        for (int j = 0; j < kMaxJ; ++j) {
+          const int r = r_begin + j * kEpiWarps;
+          res[j] = r < r_end
+                       ? __ldg(reinterpret_cast<const float4*>(g.ep.residual + (row0 + r) * g.ep.residual_ld + n0 + c4))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
     if constexpr (M == kAPlanes) {
       if (ct < R) exp_s[ct] = ct < valid ? g.row_exp[blockIdx.y * g.m + row0 + ct] : 0;
       if (nkb > 0) ok &= MbarWaitSleep(&accf, 0);
@@ -541,26 +575,9 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   // tiles in rank order (deterministic) through distributed shared memory.
   const int splits = static_cast<int>(gridDim.y);
   const int64_t rows = Min64(R, g.m - row0);
+  int r_begin, r_end;
+  split_rows(&r_begin, &r_end);
   float* tile = reinterpret_cast<float*>(smem);  // [R][kBn], over the stages
-  // Split K: rank `rank` sums rows [rank * rpr, +rpr) of the tile over the
-  // cluster; a thread owns one group of four columns (lane) in rows tid / 32,
-  // + warps, ... Its residual rows are loaded now, so that their latency
-  // overlaps the accumulator read-out and the cluster reduction.
-  const int rank = static_cast<int>(blockIdx.y);  // cluster (1, splits, 1): rank = y
-  const int rpr = (static_cast<int>(rows) + splits - 1) / splits;
-  const int r_begin = rank * rpr + warp;
-  const int r_end = min(static_cast<int>(rows), (rank + 1) * rpr);
-  constexpr int kMaxJ = (R / 2 + kThreads / 32 - 1) / (kThreads / 32);  // rows per thread (splits >= 2)
-  float4 res[kEarly ? kMaxJ : 1];
-  const bool res_pre = kEarly && splits > 1 && g.res_vec && !g.silu_pairs && c4 + 4 <= cols;
-  if (res_pre) {
-#pragma unroll
-    for (int j = 0; j < (kEarly ? kMaxJ : 1); ++j) {
-      const int r = r_begin + j * (kThreads / 32);
-      res[j] = r < r_end ? __ldg(reinterpret_cast<const float4*>(g.ep.residual + (row0 + r) * g.ep.residual_ld + n0 + c4))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
   if (warp >= 2) {
     // Thread (quarter, lane) holds feature 32 * quarter + lane: its TMEM lane.
     // Column p * R + r holds digit plane p of row r. With eight converter
@@ -662,7 +679,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   if (c4 < cols) {
 #pragma unroll
     for (int j = 0; j < kMaxJ; ++j) {
-      const int r = r_begin + j * (kThreads / 32);
+      const int r = r_begin + j * kEpiWarps;
       if (r < r_end) {
         // Summed over ranks 0, 1, ... in order: the result does not depend on
         // which rank finished first.
@@ -690,7 +707,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 #pragma unroll
   for (int j = 0; j < kMaxJ; ++j) {
-    const int r = r_begin + j * (kThreads / 32);  // the same for the 32 lanes of a warp
+    const int r = r_begin + j * kEpiWarps;  // the same for the 32 lanes of a warp
     if (r < r_end && g.silu_pairs) {
       StoreSiluPairs(g.c, g.ldc, g.vec_store, row0 + r, n0, lane, sum[j], sc);
     } else if (r < r_end) {
@@ -703,7 +720,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
           // The residual comes last in the epilogue (ApplyEpilogue's order).
           Epilogue head = g.ep;
           head.residual = nullptr;
-          const float4 rj = res[kEarly ? j : 0];
+          const float4 rj = res[kEarly ? j : 0];  // loaded after the wait (converter branch)
           const float rv[4] = {rj.x, rj.y, rj.z, rj.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
