@@ -88,9 +88,10 @@ __device__ __forceinline__ void PrefetchShare(const accel_b200_l2_prefetch& pf) 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a) {
   extern __shared__ __align__(128) float buf[];  // [2][K | V][64 rows][64]
-  __shared__ __align__(8) uint64_t full[2], empty[2];
+  __shared__ __align__(8) uint64_t full[2], full_v[2], empty[2];  // keys landed, values landed, buffer free
   __shared__ __align__(16) float qs[G * kD];        // roped query heads
   __shared__ __align__(16) float wo[kWarps][G * kD];  // per-warp weighted values
+  __shared__ __align__(16) float ps[kWarps][G][kRows / kWarps];  // per-warp weights of the chunk's rows
   __shared__ float wm[kWarps][G], wl[kWarps][G];    // per-warp running max and sum
   __shared__ __align__(16) float mo[G * kD];        // published weighted values
   __shared__ float m_run[G], l_run[G];
@@ -120,30 +121,35 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   if (tid == 0) {
     for (int b = 0; b < 2; ++b) {
       MbarInit(&full[b], 1);
+      MbarInit(&full_v[b], 1);
       MbarInit(&empty[b], kWarps);
     }
     FenceBarrierInit();
   }
   __syncthreads();
 
-  // Issues the copies of local chunk i into buffer i & 1. The new row (the
-  // last of the context) is not copied: the owner writes it.
+  // Issues the copies of local chunk i into buffer i & 1, keys and values on
+  // their own barriers (the scores need only the keys). The new row (the last
+  // of the context) is not copied: the owner writes it.
   auto issue = [&](int i) {
     const int64_t t0 = static_cast<int64_t>(c_begin + i) * kRows;
     const int64_t cnt = Min64(kRows, len - t0);
     const int64_t copy = t0 + cnt == len ? cnt - 1 : cnt;
     float* kb = buf + (i & 1) * 2 * kChunkFloats;
-    uint64_t* bar = &full[i & 1];
+    uint64_t* bar_k = &full[i & 1];
+    uint64_t* bar_v = &full_v[i & 1];
     if (copy > 0) {
       // Read once per step: evict first, ahead of the weights the layer's
       // products read next.
       const uint32_t bytes = static_cast<uint32_t>(copy) * kD * 4;
       const uint64_t policy = EvictFirstPolicy();
-      MbarArriveExpectTx(bar, 2 * bytes);
-      BulkCopyG2SHint(kb, kbase + t0 * kD, bytes, bar, policy);
-      BulkCopyG2SHint(kb + kChunkFloats, vbase + t0 * kD, bytes, bar, policy);
+      MbarArriveExpectTx(bar_k, bytes);
+      BulkCopyG2SHint(kb, kbase + t0 * kD, bytes, bar_k, policy);
+      MbarArriveExpectTx(bar_v, bytes);
+      BulkCopyG2SHint(kb + kChunkFloats, vbase + t0 * kD, bytes, bar_v, policy);
     } else {
-      MbarArrive(bar);
+      MbarArrive(bar_k);
+      MbarArrive(bar_v);
     }
   };
   if (tid == 0) {
@@ -168,10 +174,12 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
 
   // Warp w owns rows 16w .. 16w + 15 of every chunk and keeps its own online
   // softmax: lane pair (2j, 2j + 1) scores row 16w + j (each lane over half of
-  // the dimensions), and every lane accumulates dimensions lane and lane + 32
-  // of the weighted values for all G heads. No CTA barrier per chunk: a warp
-  // frees a buffer through `empty`, and the producer (thread 0) refills it once
-  // all four warps are done with it.
+  // the dimensions); the pair's even lane puts the row's weights in shared
+  // memory, from which every lane reads four rows' weights per head at once,
+  // and lane l accumulates dimensions 2l and 2l + 1 of the weighted values for
+  // all G heads. No CTA barrier per chunk: a warp frees a buffer through
+  // `empty`, and the producer (thread 0) refills it once all four warps are
+  // done with it.
   constexpr int kWarpRows = kRows / kWarps;
   const int wr0 = warp * kWarpRows;
   float m_w[G], l_w[G], o[G][2];
@@ -248,17 +256,34 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
         o[hh][1] *= corr;
       }
       const int rows = min(kWarpRows, cnt - wr0);
-#pragma unroll 4
-      for (int rr = 0; rr < rows; ++rr) {
-        const float v0 = vb[(wr0 + rr) * kD + lane];
-        const float v1 = vb[(wr0 + rr) * kD + lane + 32];
+      ok &= MbarWait(&full_v[i & 1], (i >> 1) & 1);
+      if (half == 0) {
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          const float pr = __shfl_sync(kFull, p[hh], 2 * rr);
-          o[hh][0] = fmaf(pr, v0, o[hh][0]);
-          o[hh][1] = fmaf(pr, v1, o[hh][1]);
+        for (int hh = 0; hh < G; ++hh) ps[warp][hh][lane >> 1] = p[hh];
+      }
+      __syncwarp();
+      for (int r4 = 0; r4 < rows; r4 += 4) {
+        float4 pw[G];
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) pw[hh] = *reinterpret_cast<const float4*>(&ps[warp][hh][r4]);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          if (r4 + t < rows) {
+            const float2 v = *reinterpret_cast<const float2*>(vb + (wr0 + r4 + t) * kD + 2 * lane);
+#pragma unroll
+            for (int hh = 0; hh < G; ++hh) {
+              const float pr = t == 0 ? pw[hh].x : t == 1 ? pw[hh].y : t == 2 ? pw[hh].z : pw[hh].w;
+              o[hh][0] = fmaf(pr, v.x, o[hh][0]);
+              o[hh][1] = fmaf(pr, v.y, o[hh][1]);
+            }
+          }
         }
       }
+      __syncwarp();  // the weights are read before the next chunk rewrites them
+    } else {
+      // No rows of this (last) chunk: still see its values land, so that no
+      // copy is in flight into a buffer this warp has released.
+      ok &= MbarWait(&full_v[i & 1], (i >> 1) & 1);
     }
     __syncwarp();
     if (lane == 0) MbarArrive(&empty[i & 1]);
@@ -271,13 +296,16 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   if (!ok) {
     if (tid == 0 && a.status != nullptr) atomicOr(a.status, ACCEL_B200_STATUS_COPY_TIMEOUT);
     // Copies still in flight land before the CTA leaves (bounded waits).
-    for (int i = 0; i < nloc && i < 2; ++i) MbarWait(&full[i & 1], ((nloc - 1 - i) >> 1) & 1);
+    for (int i = 0; i < nloc && i < 2; ++i) {
+      MbarWait(&full[i & 1], ((nloc - 1 - i) >> 1) & 1);
+      MbarWait(&full_v[i & 1], ((nloc - 1 - i) >> 1) & 1);
+    }
   }
   // The four warp states -> one CTA state (log-sum-exp, warps in order).
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
-    wo[warp][hh * kD + lane] = o[hh][0];
-    wo[warp][hh * kD + lane + 32] = o[hh][1];
+    wo[warp][hh * kD + 2 * lane] = o[hh][0];
+    wo[warp][hh * kD + 2 * lane + 1] = o[hh][1];
     if (lane == 0) {
       wm[warp][hh] = m_w[hh];
       wl[warp][hh] = l_w[hh];
