@@ -44,11 +44,11 @@ WEIGHT_SEED = 4
 PROMPT_SEED = 41
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
-# DRAM bytes (read + write) per launch from ncu captures of the same launches
-# (profiles/q8_product_decode_qkv_m32.md: one decode step's products, 168.2 MB
-# over 121 products; profiles/decode_attention_b32_len1280.md).
-PRODUCT_TRAFFIC = 1_390_285
-ATTENTION_TRAFFIC = 63_610_368
+# DRAM bytes (read + write) per launch from ncu captures of the same kernels
+# (profiles/q8_product_decode_qkv_m32.md: per product kind, weighted by the
+# step's launches, 158.0 MB over 121 products; profiles/decode_attention_b32_len1280.md).
+PRODUCT_TRAFFIC = 1_305_636
+ATTENTION_TRAFFIC = 63_622_400
 GEMV_TRAFFIC = 274_861_568  # profiles/q8_gemv_c5_m1_k16384.md
 
 
