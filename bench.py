@@ -329,6 +329,31 @@ def attention_roofline(torch, stream, batch=SEQS, length=1280, reps=50):
     return nbytes / sec / 1e9, sec, nbytes
 
 
+def step_roofline(torch, model, prompts, stream, job_sec, new, peak):
+    """The whole decode step against HBM: the job's time minus its prefill
+    (a generate of 0 new ids, timed the same way), per decode step, against
+    the bytes one step must move at the job's mean context: the int8 weights
+    and scales once, every sequence's key and value rows up to its position
+    read, the new rows written."""
+    model.generate_batch(prompts, 0)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(3):
+        model.generate_batch(prompts, 0)
+    end.record(stream)
+    end.synchronize()
+    prefill = start.elapsed_time(end) / 1e3 / 3
+    step = (job_sec - prefill) / new
+    kv_row = 30 * 2 * 3 * 64 * 4  # bytes of one position's keys and values over the 30 layers
+    mean_ctx = len(prompts[0]) + (new + 1) / 2.0
+    nbytes = 134_479_872 + 818_688 + SEQS * mean_ctx * kv_row + SEQS * kv_row
+    return {"what": "one C4 decode step (job time minus prefill, / new ids) against the bytes it must move at the "
+                    "mean context (weights and scales once, KV rows read, new rows written)",
+            "prefill_ms": prefill * 1e3, "decode_step_us": step * 1e6, "bytes_per_step": nbytes,
+            "achieved": nbytes / step / 1e9, "peak": peak, "unit": "GB/s", "frac": nbytes / step / 1e9 / peak,
+            "roofline_tok_s": SEQS * peak * 1e9 / nbytes}
+
+
 def products_roofline(torch, stream, reps=3):
     """Times the decode step's 121 int8 products (C4 shapes, synthetic weights)
     replayed from one CUDA graph, with CUDA events on the launching stream;
@@ -574,6 +599,7 @@ def run_b200(args):
 
     if rank == 0:
         peak, peak_kind = hbm_peak()
+        step_line = step_roofline(torch, model, prompts, stream, dev_sec / args.steps, new, peak)
         achieved, sec, nbytes = attention_roofline(torch, stream)
         p_achieved, p_sec, p_bytes = products_roofline(torch, stream)
         gemv = gemv_roofline(torch)
@@ -612,7 +638,7 @@ def run_b200(args):
                                        "transpose; fused: peer stores from the product epilogue + peer-memory "
                                        "barrier); max over ranks", "ranks": world, "points": sharded_rows,
                                "clocks": c5_clk},
-                "metric_set": extras, "cpu_baseline": cpu, "clocks": clk}
+                "step_roofline": step_line, "metric_set": extras, "cpu_baseline": cpu, "clocks": clk}
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:
