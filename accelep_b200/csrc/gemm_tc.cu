@@ -95,14 +95,18 @@ constexpr int ConvWarps() { return (M == 0 && R < 64) ? 4 : 8; }
 template <int R, int M>
 constexpr int Threads() { return (2 + ConvWarps<R, M>()) * 32; }
 
-enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2, kANorm = 3 };
+// Operand modes. The kernel is instantiated for kAPlanes and for kAIn (the
+// in-kernel operand), whose form — plain, SiluMul or RmsNorm rows — is a
+// runtime argument (TcArgs::amode): one kernel body serves every decode
+// product, so the code the SMs fetch for one product is warm for the next.
+enum AMode : int { kAPlanes = 0, kAF32 = 1, kASilu = 2, kANorm = 3, kAIn = 4 };
 
 template <int R, int S, int M>
 struct Tc {
   static constexpr int kXBytes = kDigits * R * kBk;  // digit planes of one k block (MMA B operand)
   static constexpr int kStage = kXBytes + kWBytes;   // digits, then the weight block; 1024-aligned
   static constexpr int kStages = S;
-  static constexpr int kYTiles = M == kAPlanes ? 0 : (M == kASilu ? 2 : 1);  // fp32 tiles per k block
+  static constexpr int kYTiles = M == kAPlanes ? 0 : 2;  // fp32 tiles per k block (A, and up for SiluMul)
   static constexpr int kYTile = R * kBk * 4;                                  // one fp32 tile [R][128 k]
   static constexpr int kYBytes = kYTiles * kInKernelBlocks * kYTile;
   static constexpr int kTile = R * kBn * 4;  // fp32 accumulator tile, over the stages after the main loop
@@ -114,6 +118,7 @@ struct Tc {
 };
 
 struct TcArgs {
+  int32_t amode;       // kAIn: how the operand rows are formed (kAF32, kASilu or kANorm)
   const float* a;      // fp32 A rows (norm mode: the whole rows are read for their RMS)
   const float* up;     // silu mode: the up rows (row stride lda)
   int64_t lda;
@@ -268,24 +273,25 @@ __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int6
 // keep a warp's formed rows in registers between the maxima and the digits
 // (all of a warp's shared-memory loads issue back to back); 64-row tiles
 // write the formed rows back in place and read them again.
-template <int R, int M, int CW>
+template <int R, int CW>
 __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0, const double* inv, float* ytiles,
                                             uint32_t* amax, int32_t* exp_s, uint8_t* stages, int stage_bytes,
                                             int ct) {
-  constexpr int kTiles = M == kASilu ? 2 : 1;
+  const int mode = g.amode;
+  const int kTiles = mode == kASilu ? 2 : 1;
   const int w = ct >> 5, lane = ct & 31;
   const int b = w % nkb, r0 = w / nkb, rstep = CW / nkb;
   const int kb = 4 * lane;  // k offset inside the block
   float* y_at = ytiles + b * kTiles * R * kBk + kb;
   float4 gam = make_float4(0.f, 0.f, 0.f, 0.f);
-  if constexpr (M == kANorm) {
+  if (mode == kANorm) {
     if (k0 + b * kBk + kb < g.k) gam = __ldg(reinterpret_cast<const float4*>(g.gamma + k0 + b * kBk + kb));
   }
   const auto form = [&](float4 v, int r) {
-    if constexpr (M == kASilu) {
+    if (mode == kASilu) {
       const float4 u = *reinterpret_cast<const float4*>(y_at + R * kBk + r * kBk);
       return make_float4(SiluMul(v.x, u.x), SiluMul(v.y, u.y), SiluMul(v.z, u.z), SiluMul(v.w, u.w));
-    } else if constexpr (M == kANorm) {
+    } else if (mode == kANorm) {
       const double iv = inv[r];
       return make_float4(__fmul_rn(static_cast<float>(static_cast<double>(v.x) * iv), gam.x),
                          __fmul_rn(static_cast<float>(static_cast<double>(v.y) * iv), gam.y),
@@ -344,7 +350,7 @@ __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0
     for (int r = r0; r < R; r += rstep) {
       float4* at = reinterpret_cast<float4*>(y_at + r * kBk);
       const float4 y = form(*at, r);
-      if constexpr (M != kAF32) *at = y;
+      if (mode != kAF32) *at = y;
       const uint32_t m = __reduce_max_sync(kFull, AbsMaxBits(y));
       if (lane == 0) amax[2 * r + b] = m;
     }
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   __shared__ uint32_t tmem_s;
   __shared__ int32_t exp_s[R];
   __shared__ uint32_t amax_s[M == kAPlanes ? 1 : 2 * R];
-  __shared__ double inv_s[M == kANorm ? R : 1];
+  __shared__ double inv_s[M == kAPlanes ? 1 : R];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t raw_addr = SmemAddr(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
@@ -469,12 +475,13 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
         // The fp32 tiles of every k block of the CTA, one barrier per block.
         PdlWait();
         float* ytiles = reinterpret_cast<float*>(smem + S * L::kStage);
+        const int tiles = g.amode == kASilu ? 2 : 1;
         for (int i = 0; i < nkb; ++i) {
           const int32_t k0 = (kb_begin + i) * kBk;
-          float* dst = ytiles + i * L::kYTiles * R * kBk;
-          MbarArriveExpectTx(&full_x[i], L::kYTiles * L::kYTile);
+          float* dst = ytiles + i * tiles * R * kBk;
+          MbarArriveExpectTx(&full_x[i], static_cast<uint32_t>(tiles * L::kYTile));
           TmaLoad2D(dst, &tx, k0, static_cast<int32_t>(row0), &full_x[i]);
-          if constexpr (M == kASilu) TmaLoad2D(dst + R * kBk, &tu, k0, static_cast<int32_t>(row0), &full_x[i]);
+          if (tiles == 2) TmaLoad2D(dst + R * kBk, &tu, k0, static_cast<int32_t>(row0), &full_x[i]);
         }
       }
     }
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
       if (ct < R) exp_s[ct] = ct < valid ? g.row_exp[blockIdx.y * g.m + row0 + ct] : 0;
       if (nkb > 0) ok &= MbarWaitSleep(&accf, 0);
     } else {
-      if constexpr (M == kANorm) {
+      if (g.amode == kANorm) {
         // Row RMS of the valid rows: from the producer's sums of squares when
         // given, else from the whole rows of A.
         if (g.sq_in != nullptr) {
@@ -550,7 +557,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
         asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
       }
       for (int i = 0; i < nkb; ++i) ok &= MbarWaitSleep(&full_x[i], 0);
-      BuildDigits<R, M, kConvWarps>(g, nkb, static_cast<int64_t>(kb_begin) * kBk, inv_s,
+      BuildDigits<R, kConvWarps>(g, nkb, static_cast<int64_t>(kb_begin) * kBk, inv_s,
                         reinterpret_cast<float*>(smem + S * L::kStage), amax_s, exp_s, smem, L::kStage, ct);
       FenceProxyAsyncSmem();
       __syncwarp();
@@ -923,14 +930,14 @@ int LaunchTc(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu
                        "matmul_q8_tc");
 }
 
-// In-kernel operand modes (m <= 64).
-template <int M>
+// In-kernel operand modes (m <= 64): one instantiation per tile height, the
+// mode in TcArgs::amode.
 int LaunchTcRows(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tu, const TcArgs& g,
                  const TcPlan& p, cudaStream_t s) {
   switch (p.r) {
-    case 16: return LaunchTc<16, kInKernelBlocks, M>(tw, tx, tu, g, p, s);
-    case 32: return LaunchTc<32, kInKernelBlocks, M>(tw, tx, tu, g, p, s);
-    default: return LaunchTc<64, kInKernelBlocks, M>(tw, tx, tu, g, p, s);
+    case 16: return LaunchTc<16, kInKernelBlocks, kAIn>(tw, tx, tu, g, p, s);
+    case 32: return LaunchTc<32, kInKernelBlocks, kAIn>(tw, tx, tu, g, p, s);
+    default: return LaunchTc<64, kInKernelBlocks, kAIn>(tw, tx, tu, g, p, s);
   }
 }
 
@@ -1075,9 +1082,9 @@ int RunTc(const float* a, const float* up, int64_t lda, const float* gamma, floa
   }
   switch (p.mode) {
     case kAPlanes: return LaunchTcPlanes(tw, tx, g, p, stream);
-    case kASilu: return LaunchTcRows<kASilu>(tw, tx, tu, g, p, stream);
-    case kANorm: return LaunchTcRows<kANorm>(tw, tx, tu, g, p, stream);
-    default: return LaunchTcRows<kAF32>(tw, tx, tu, g, p, stream);
+    default:
+      g.amode = p.mode;
+      return LaunchTcRows(tw, tx, tu, g, p, stream);
   }
 }
 
