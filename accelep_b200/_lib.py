@@ -30,13 +30,13 @@ class Epilogue(ctypes.Structure):
 
     _fields_ = [("alpha", c_f32), ("beta", c_f32), ("bias", c_vp), ("bias_row_stride", c_i64),
                 ("bias_col_stride", c_i64), ("act", c_i32), ("residual", c_vp), ("residual_ld", c_i64),
-                ("row_sq", c_vp), ("row_sq_ld", c_i64)]
+                ("row_sq", c_vp), ("row_sq_ld", c_i64), ("flags", c_i32)]
 
 
 class L2Prefetch(ctypes.Structure):
     """accel_b200_l2_prefetch (include/accel_b200.h)."""
 
-    _fields_ = [("ptr", c_vp * 4), ("bytes", c_i64 * 4), ("count", c_i32)]
+    _fields_ = [("ptr", c_vp * 4), ("bytes", c_i64 * 4), ("count", c_i32), ("flags", c_i32)]
 
 
 class LlamaConfig(ctypes.Structure):

@@ -130,6 +130,7 @@ struct Epilogue {
   int64_t residual_ld = 0;
   double* row_sq = nullptr;  // per row and 128-column block: sum of squares of the outputs
   int64_t row_sq_ld = 0;
+  int32_t flags = 0;  // ACCEL_B200_EP_TRIGGER_AFTER_WAIT
 };
 
 __device__ __forceinline__ float ApplyEpilogue(const Epilogue& ep, float acc, int64_t i, int64_t j) {

@@ -99,7 +99,13 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
   // Ranges for later kernels (immutable weights) go to L2 while this kernel
   // waits for its inputs.
   if (threadIdx.x == 0 && a.prefetch.count > 0) PrefetchShare(a.prefetch);
-  PdlWait();  // row positions, q|k|v rows and the cache come from earlier kernels
+  // The q|k|v rows come from the previous kernel. The row positions, slots
+  // and cache rows come from kernels before it: with CACHE_BEFORE_WAIT those
+  // have completed when this kernel starts (the previous kernel let it launch
+  // only after its own wait), so they are read, and the first chunks' copies
+  // issued, before the wait.
+  const bool early = (a.prefetch.flags & ACCEL_B200_ATTN_CACHE_BEFORE_WAIT) != 0;
+  if (!early) PdlWait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rank = static_cast<int>(blockIdx.x), S = static_cast<int>(gridDim.x);
   const int g = static_cast<int>(blockIdx.y);
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
     if (nloc > 0) issue(0);
     if (nloc > 1) issue(1);
   }
+  if (early) PdlWait();
 
   // RoPE of the G query heads into shared memory (all ranks need them).
   if (pos >= 0) {
@@ -425,7 +432,9 @@ ACCEL_B200_API int accel_b200_decode_attention_prefetch(
   if (group > kMaxG) return SetError(ACCEL_B200_EINVAL, "decode_attention: more than 8 query heads per kv head");
   accel_b200_l2_prefetch pf{};
   if (prefetch != nullptr) {
-    if (prefetch->count < 0 || prefetch->count > 4) return SetError(ACCEL_B200_EINVAL, "decode_attention: bad prefetch");
+    if (prefetch->count < 0 || prefetch->count > 4 || (prefetch->flags & ~ACCEL_B200_ATTN_CACHE_BEFORE_WAIT) != 0) {
+      return SetError(ACCEL_B200_EINVAL, "decode_attention: bad prefetch");
+    }
     for (int i = 0; i < prefetch->count; ++i) {
       if (prefetch->bytes[i] < 0 || (prefetch->bytes[i] > 0 && prefetch->ptr[i] == nullptr) ||
           reinterpret_cast<uintptr_t>(prefetch->ptr[i]) % 16 != 0) {

@@ -318,7 +318,8 @@ bool ToEpilogue(const accel_b200_epilogue* in, Epilogue* out) {
   out->residual_ld = in->residual_ld;
   out->row_sq = in->row_sq;
   out->row_sq_ld = in->row_sq_ld;
-  return in->act >= 0 && in->act <= 2;
+  out->flags = in->flags;
+  return in->act >= 0 && in->act <= 2 && (in->flags & ~ACCEL_B200_EP_TRIGGER_AFTER_WAIT) == 0;
 }
 
 // Zero-size products still define C: an empty sum is 0 before the epilogue.
@@ -389,7 +390,7 @@ int MatMulQ8(const float* a, int64_t lda, const accel_b200_q8_plane* b, float* c
   if (m < 0 || k < 0 || n < 0 || b == nullptr) return SetError(ACCEL_B200_EINVAL, "quantized MatMul is out of range");
   if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
   GemmArgs g{};
-  if (!ToEpilogue(ep, &g.ep)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
+  if (!ToEpilogue(ep, &g.ep)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation or flags");
   if (m == 0 || n == 0) return ClearError();
   if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
   const bool with_peers = peers != nullptr && peers->n > 0;
@@ -500,7 +501,7 @@ ACCEL_B200_API int accel_b200_matmul_q8_silu(const float* gate_up, int64_t ld, i
   }
   if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
   Epilogue e{};
-  if (!ToEpilogue(ep, &e)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
+  if (!ToEpilogue(ep, &e)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation or flags");
   if (m == 0 || n == 0) return ClearError();
   if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
   if (inter == 0) return EmptySum(c, ldc, m, n, e, AsStream(stream));
@@ -540,7 +541,7 @@ static int MatMulQ8RmsNorm(const float* x, int64_t ldx, const double* sq, int64_
   }
   if (b->axis < -1 || b->axis > 1 || b->offset < 0) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad plane axis");
   Epilogue e{};
-  if (!ToEpilogue(ep, &e)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation");
+  if (!ToEpilogue(ep, &e)) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad activation or flags");
   if (m == 0 || n == 0) return ClearError();
   if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "quantized MatMul: bad output");
   if (k == 0) return EmptySum(c, ldc, m, n, e, AsStream(stream));
@@ -619,7 +620,7 @@ ACCEL_B200_API int accel_b200_matmul_f32(const float* a, int64_t lda, const floa
                                          size_t workspace_bytes, void* stream) {
   if (m < 0 || k < 0 || n < 0) return SetError(ACCEL_B200_EINVAL, "MatMul is out of range");
   GemmArgs g{};
-  if (!ToEpilogue(ep, &g.ep)) return SetError(ACCEL_B200_EINVAL, "MatMul: bad activation");
+  if (!ToEpilogue(ep, &g.ep)) return SetError(ACCEL_B200_EINVAL, "MatMul: bad activation or flags");
   if (m == 0 || n == 0) return ClearError();
   if (c == nullptr || ldc < n) return SetError(ACCEL_B200_EINVAL, "MatMul: bad output");
   if (k == 0) return EmptySum(c, ldc, m, n, g.ep, AsStream(stream));

@@ -393,7 +393,15 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   const int kb_begin = blockIdx.y * g.kb_per_split;
   const int nkb = max(0, min(g.kb_total, kb_begin + g.kb_per_split) - kb_begin);
 
-  PdlTrigger();
+  // The next kernel may launch at once, or (TRIGGER_AFTER_WAIT) only once a
+  // thread of this CTA has waited for the previous kernel: then every kernel
+  // before this one has completed when the next one starts.
+  const bool late = (g.ep.flags & ACCEL_B200_EP_TRIGGER_AFTER_WAIT) != 0;
+  if (!late) PdlTrigger();
+  const auto wait_prev = [late] {
+    PdlWait();
+    if (late) PdlTrigger();
+  };
   if (warp == 1) TmemAlloc(&tmem_s, kCols);
   // The epilogue's column scales, lane l's four columns 4l .. 4l + 3 of the
   // tile in every warp. The latency-bound in-kernel modes load them here
@@ -458,7 +466,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
         TmaLoad2D(smem + i * L::kStage + L::kXBytes, &tw, static_cast<int32_t>(n0), (kb_begin + i) * kBk, &full_w[i]);
       }
       if constexpr (M == kAPlanes) {
-        PdlWait();
+        wait_prev();
         for (int i = 0; i < nkb; ++i) {
           const int s = i % S;
           uint8_t* stage = smem + s * L::kStage;
@@ -473,7 +481,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
         }
       } else {
         // The fp32 tiles of every k block of the CTA, one barrier per block.
-        PdlWait();
+        wait_prev();
         float* ytiles = reinterpret_cast<float*>(smem + S * L::kStage);
         const int tiles = g.amode == kASilu ? 2 : 1;
         for (int i = 0; i < nkb; ++i) {
@@ -490,7 +498,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
       // Nothing for the MMA arrives before the previous kernel completes: wait
       // in griddepcontrol.wait (no issue slots) rather than polling barriers
       // while that kernel still runs on this SM.
-      PdlWait();
+      wait_prev();
       // Suspended, not polling: a polling warp would compete for the shared
       // memory pipe with the converter warps that form the operand meanwhile.
       if constexpr (M != kAPlanes) ok &= MbarWaitSleep(&xready, 0);
@@ -522,7 +530,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   } else {
     const int ct = tid - 64;
     const int valid = static_cast<int>(Min64(R, g.m - row0));
-    PdlWait();
+    wait_prev();
     if constexpr (kEarly) {
       if (res_pre) {
         int r_begin, r_end;
@@ -566,7 +574,7 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
     }
   }
   // Every thread past this point may read the residual or write the output.
-  PdlWait();
+  wait_prev();
   const bool cta_ok = __syncthreads_and(ok);
   if (!cta_ok) {
     // A wait ran out: report it and let the tensor core finish (bounded). The

@@ -85,7 +85,10 @@ __global__ void __launch_bounds__(kGvThreads) Q8GemvKernel(GemvArgs g) {
   constexpr int SW = 32 * CPL;  // columns per CTA
   extern __shared__ __align__(16) float red[];  // [kGvWarps][MT][SW], then the CTA sum [MT][SW]
   float* cta_sum = red + kGvWarps * MT * SW;
-  PdlTrigger();
+  // The next kernel may launch at once, or (TRIGGER_AFTER_WAIT) only after
+  // this CTA has waited for the previous kernel.
+  const bool late = (g.ep.flags & ACCEL_B200_EP_TRIGGER_AFTER_WAIT) != 0;
+  if (!late) PdlTrigger();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rank = static_cast<int>(blockIdx.y), splits = static_cast<int>(gridDim.y);
   const int64_t strip0 = static_cast<int64_t>(blockIdx.x) * SW;
@@ -100,6 +103,7 @@ __global__ void __launch_bounds__(kGvThreads) Q8GemvKernel(GemvArgs g) {
 #pragma unroll
     for (int c = 0; c < CPL; ++c) acc[r][c] = 0.f;
   PdlWait();  // A comes from an earlier kernel
+  if (late) PdlTrigger();
   if (col0 < g.n) {
     // Two register buffers: the loads of batch i + 1 are in flight while batch
     // i is converted and accumulated.

@@ -726,8 +726,18 @@ class Engine {
       Layer& l = layers[static_cast<size_t>(li)];
       float* kc = k_cache[static_cast<size_t>(li)].as<float>();
       float* vc = v_cache[static_cast<size_t>(li)].as<float>();
-      NormGemm(hid, l.attn_norm, l.qkv, rows, qkv.as<float>(), qkv_ld, nullptr, normed, li > 0 ? sq : nullptr);
-      if (decode && head_dim == 64) {
+      // Decode: the q|k|v product lets the attention launch only after its
+      // own wait, so the attention reads the cache (written by earlier
+      // kernels, all completed by then) and starts its first copies before
+      // it waits for the q|k|v rows.
+      const bool fused = decode && head_dim == 64;
+      accel_b200_epilogue qkv_ep{};
+      qkv_ep.alpha = 1.f;
+      qkv_ep.flags = ACCEL_B200_EP_TRIGGER_AFTER_WAIT;
+      const bool early = fused && l.qkv.kind == WKind::Q8;
+      NormGemm(hid, l.attn_norm, l.qkv, rows, qkv.as<float>(), qkv_ld, early ? &qkv_ep : nullptr, normed,
+               li > 0 ? sq : nullptr);
+      if (fused) {
         // Rope, AppendCache and attention of the new rows in one kernel.
         // While it runs, the int8 weights of the products that follow (this
         // layer's o, gate|up and down, then the next layer's q|k|v or, after
@@ -741,6 +751,7 @@ class Engine {
           pf.bytes[pf.count] = g->k * g->n;
           ++pf.count;
         }
+        if (early) pf.flags = ACCEL_B200_ATTN_CACHE_BEFORE_WAIT;
         Abi(accel_b200_decode_attention_prefetch(qkv.as<float>(), qkv_ld, rseq, rpos, rows, cfg.heads, cfg.kv_heads,
                                                  head_dim, rope_cos.as<float>(), rope_sin.as<float>(), cfg.context,
                                                  kc, vc, slot_stride, head_stride, mixed.as<float>(), q_out,

@@ -105,9 +105,15 @@ def gemm_epilogue(c, alpha, bias, bias_shape, beta, act):
     return c
 
 
-def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none", residual=None, row_sq=None):
+EP_TRIGGER_AFTER_WAIT = 1  # ACCEL_B200_EP_TRIGGER_AFTER_WAIT
+ATTN_CACHE_BEFORE_WAIT = 1  # ACCEL_B200_ATTN_CACHE_BEFORE_WAIT
+
+
+def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none", residual=None, row_sq=None,
+                  flags=0):
     """row_sq: a float64 [m, ceil(n / 128)] tensor that receives each row's
-    sums of squares of the outputs per 128-column block."""
+    sums of squares of the outputs per 128-column block. flags: launch
+    options (EP_TRIGGER_AFTER_WAIT)."""
     ep = Epilogue()
     ep.alpha, ep.beta = alpha, beta
     ep.bias = 0 if bias is None else bias.data_ptr()
@@ -117,6 +123,7 @@ def make_epilogue(alpha=1.0, beta=0.0, bias=None, bias_strides=(0, 0), act="none
     ep.residual_ld = 0 if residual is None else residual.stride(0)
     ep.row_sq = 0 if row_sq is None else row_sq.data_ptr()
     ep.row_sq_ld = 0 if row_sq is None else row_sq.stride(0)
+    ep.flags = flags
     # The struct holds raw addresses: keep the tensors alive with it.
     ep._keep = (bias, residual, row_sq)
     return ep
@@ -286,24 +293,26 @@ def rope_append(qkv, row_seq, row_pos, heads, kv_heads, head_dim, cos_t, sin_t, 
 
 
 def decode_attention(qkv, row_pos, heads, kv_heads, cos_t, sin_t, k_cache, v_cache, row_seq=None, out=None,
-                     status=None, prefetch=None):
+                     status=None, prefetch=None, flags=0):
     """Fused decode step (Rope, AppendCache, attention) over un-rotated q|k|v
     rows; caches head-major [slots, kv_heads, context, 64]. prefetch: up to
-    four contiguous device tensors to bring into L2 meanwhile (a hint)."""
+    four contiguous device tensors to bring into L2 meanwhile (a hint).
+    flags: launch options (ATTN_CACHE_BEFORE_WAIT)."""
     rows, ctx = qkv.shape[0], k_cache.shape[2]
     if out is None:
         out = torch.zeros(rows, heads * 64, dtype=torch.float32, device=qkv.device)
     args = (_p(qkv), qkv.stride(0), _p(row_seq), _p(row_pos), rows, heads, kv_heads, 64, _p(cos_t), _p(sin_t), ctx,
             _p(k_cache), _p(v_cache), kv_heads * ctx * 64, ctx * 64, _p(out), out.stride(0), _p(status))
-    if prefetch is None:
+    if prefetch is None and flags == 0:
         check(load().accel_b200_decode_attention(*args, _s()))
     else:
         from ._lib import L2Prefetch
         pf = L2Prefetch()
-        for i, t in enumerate(prefetch):
+        for i, t in enumerate(prefetch or []):
             pf.ptr[i] = t.data_ptr()
             pf.bytes[i] = t.numel() * t.element_size()
-        pf.count = len(prefetch)
+        pf.count = len(prefetch or [])
+        pf.flags = flags
         check(load().accel_b200_decode_attention_prefetch(*args, ctypes.byref(pf), _s()))
     return out
 

@@ -160,7 +160,16 @@ typedef struct accel_b200_epilogue {
      (accel_b200_matmul_q8_rmsnorm_stats). */
   double* row_sq;
   int64_t row_sq_ld;
+  /* Launch options (0: none). ACCEL_B200_EP_TRIGGER_AFTER_WAIT, on the GEMV
+     and tensor-core paths: the product lets the next kernel of the stream
+     launch early (programmatic dependent launch) only once it has itself
+     waited for the kernel before it, instead of at entry. When the next
+     kernel starts, every kernel before this product has then completed. No
+     effect on results. */
+  int32_t flags;
 } accel_b200_epilogue;
+
+#define ACCEL_B200_EP_TRIGGER_AFTER_WAIT 1
 
 /* Scratch, in bytes, accel_b200_matmul_q8 needs for these sizes. */
 ACCEL_B200_API size_t accel_b200_matmul_q8_workspace(int64_t m, int64_t k, int64_t n);
@@ -398,12 +407,21 @@ ACCEL_B200_API int accel_b200_decode_attention(const float* qkv, int64_t qkv_ld,
                                                void* stream);
 
 /* Up to four device ranges to bring into L2 (a hint: no completion, no
-   effect on results). */
+   effect on results), and launch options of the kernel that takes them. */
 typedef struct accel_b200_l2_prefetch {
   const void* ptr[4];
   int64_t bytes[4];
   int32_t count;
+  int32_t flags;
 } accel_b200_l2_prefetch;
+
+/* accel_b200_decode_attention_prefetch: the cache rows and the row positions
+   and slots are read before the kernel waits for the previous kernel of the
+   stream (only the q|k|v rows after it). The caller guarantees that no kernel
+   still running when this one starts writes them: the previous kernel is a
+   product launched with ACCEL_B200_EP_TRIGGER_AFTER_WAIT, a kernel that does
+   not launch its dependents early, or none. */
+#define ACCEL_B200_ATTN_CACHE_BEFORE_WAIT 1
 
 /* accel_b200_decode_attention that also brings `prefetch`'s ranges into L2
    while it waits for its inputs and streams the cache (the engine passes the

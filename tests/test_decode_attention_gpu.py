@@ -140,6 +140,46 @@ def test_decode_attention_prefetch_same_results(lib, cuda):
         K.decode_attention(T(qkv), T(pos), heads, kvh, T(cos_t), T(sin_t), T(kc), T(vc), prefetch=[weights[0][0, 1:]])
 
 
+@pytest.mark.parametrize("n_rows", [8, 32])  # the GEMV and the tensor-core product before the attention
+def test_decode_attention_cache_before_wait(lib, cuda, n_rows):
+    """The decode step as the engine launches it: a q|k|v product that lets
+    the next kernel launch only after its own wait (TRIGGER_AFTER_WAIT), then
+    the attention reading the cache before its wait (CACHE_BEFORE_WAIT).
+    Outputs and cache bits equal the plain launches'; unknown flag bits are
+    rejected."""
+    heads, kvh, hd, ctx, hidden = 9, 3, 64, 700, 576
+    rng = np.random.default_rng(14)
+    pos = np.array([0, 63, 64, 699, -1, 300, 128, 511], np.int32)
+    pos = np.concatenate([pos, rng.integers(0, ctx, n_rows - len(pos)).astype(np.int32)])
+    rows = len(pos)
+    x = rng.standard_normal((rows, hidden), dtype=np.float32)
+    w = rng.integers(-127, 128, (hidden, (heads + 2 * kvh) * hd), dtype=np.int8)
+    scale = (rng.random((heads + 2 * kvh) * hd, dtype=np.float32) + 0.5) / 256
+    kc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    vc = rng.standard_normal((rows, kvh, ctx, hd), dtype=np.float32)
+    cos_t, sin_t = tables(ctx, hd)
+    x_d, w_d, s_d = T(x), T(w), T(scale)
+    outs, caches, qkvs = [], [], []
+    for late in (False, True):
+        kc_d, vc_d = T(kc), T(vc)
+        qkv = torch.zeros(rows, (heads + 2 * kvh) * hd, device="cuda")
+        ep = K.make_epilogue(flags=K.EP_TRIGGER_AFTER_WAIT if late else 0)
+        K.matmul_q8(x_d, w_d, s_d, epilogue=ep, out=qkv)
+        out = torch.full((rows, heads * hd), 7.0, device="cuda")
+        K.decode_attention(qkv, T(pos), heads, kvh, T(cos_t), T(sin_t), kc_d, vc_d, out=out,
+                           flags=K.ATTN_CACHE_BEFORE_WAIT if late else 0)
+        outs.append(H(out))
+        qkvs.append(H(qkv))
+        caches.append((H(kc_d), H(vc_d)))
+    assert np.array_equal(qkvs[0], qkvs[1])
+    assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(caches[0][0], caches[1][0]) and np.array_equal(caches[0][1], caches[1][1])
+    with pytest.raises(B200Error):
+        K.decode_attention(T(qkvs[0]), T(pos), heads, kvh, T(cos_t), T(sin_t), T(kc), T(vc), flags=2)
+    with pytest.raises(B200Error):
+        K.matmul_q8(x_d, w_d, s_d, epilogue=K.make_epilogue(flags=2))
+
+
 def test_decode_attention_rejects(lib, cuda):
     q = torch.zeros(2, 9 * 64 + 6 * 64, device="cuda")
     kc = torch.zeros(2, 3, 16, 64, device="cuda")
