@@ -35,17 +35,19 @@
 //           exponent and writes the digit planes [4][m][kp] and the exponents
 //           [segments][m] to the workspace; TMA loads [4][R][128 k] tiles with
 //           128-byte swizzle, already the MMA's K-major canonical layout.
-//   in-kernel (up to two k blocks per CTA, R <= 64): TMA loads the CTA's fp32
-//           tiles [R rows x 128 k] (gate and up for SiluMul); the converter
-//           warps form them (SiluMul exactly as SiluMul rounds it, RmsNorm
-//           exactly as RmsNormKernel rounds it), find the exponents over the
-//           range and write the digit planes into shared memory.
+//   in-kernel (up to two k blocks per CTA, R <= 64): the converter warps
+//           load the CTA's fp32 rows (gate and up for SiluMul) straight into
+//           registers (R <= 32; at R = 64 TMA loads them as [R x 128 k]
+//           tiles into shared memory first), form them (SiluMul exactly as
+//           SiluMul rounds it, RmsNorm exactly as RmsNormKernel rounds it),
+//           find the exponents over the range and write the digit planes
+//           into shared memory.
 //
 // Pipeline (one CTA = one 128-feature x R-row tile over a range of 128-deep k
 // blocks; 6 or 10 warps):
 //   warp 0  producer: per k block one TMA of the int8 weight block [128 k x
 //           128 n] and one of the digit tile (planes) or the fp32 tile(s)
-//           (in-kernel); a ring of stages.
+//           (in-kernel, R = 64); a ring of stages.
 //   warp 1  MMA issuer (one thread): 4 k steps of 32 per block, then
 //           tcgen05.commit to the barrier that frees the stage.
 //   warps 2.. converters (eight in-kernel, four in planes mode): the
@@ -106,7 +108,9 @@ struct Tc {
   static constexpr int kXBytes = kDigits * R * kBk;  // digit planes of one k block (MMA B operand)
   static constexpr int kStage = kXBytes + kWBytes;   // digits, then the weight block; 1024-aligned
   static constexpr int kStages = S;
-  static constexpr int kYTiles = M == kAPlanes ? 0 : 2;  // fp32 tiles per k block (A, and up for SiluMul)
+  // fp32 tiles per k block (A, and up for SiluMul): in-kernel operands of
+  // more than 32 rows only (smaller tiles load their rows into registers).
+  static constexpr int kYTiles = (M == kAPlanes || R <= 32) ? 0 : 2;
   static constexpr int kYTile = R * kBk * 4;                                  // one fp32 tile [R][128 k]
   static constexpr int kYBytes = kYTiles * kInKernelBlocks * kYTile;
   static constexpr int kTile = R * kBn * 4;  // fp32 accumulator tile, over the stages after the main loop
@@ -262,21 +266,23 @@ __device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int6
   }
 }
 
-// In-kernel operand: the fp32 tiles of the CTA's k blocks (block b at
-// ytiles + b * tiles * R * 128 floats: A, then up for SiluMul; rows of 128 k;
-// rows past the matrix and k past K read as zero) are formed as the mode does,
-// the exponents over the range found (exp_s, every row of the tile), and the
+// In-kernel operand: the fp32 rows of the CTA's k blocks (rows past the
+// matrix and k past K read as zero) are formed as the mode does, the
+// exponents over the range found (exp_s, every row of the tile), and the
 // digit planes of block b written into stage b: plane p, row r at (p R + r) *
 // 128, the 16-byte chunk j of a row stored at j ^ (r % 8) (the TMA's 128-byte
 // swizzle). Converter warp w takes block w % nkb, rows w / nkb, + CW / nkb,
 // ...; lane l the quad k = 4l .. 4l + 3 of the block. Tiles of up to 32 rows
-// keep a warp's formed rows in registers between the maxima and the digits
-// (all of a warp's shared-memory loads issue back to back); 64-row tiles
-// write the formed rows back in place and read them again.
+// load their quads from global memory (row0 + r of A, and of up for SiluMul)
+// straight into registers, all of a warp's loads issued back to back, and
+// keep the formed rows there between the maxima and the digits; 64-row tiles
+// read the tiles TMA placed in shared memory (block b at ytiles + b * tiles *
+// R * 128 floats: A, then up for SiluMul; rows of 128 k), write the formed
+// rows back in place and read them again.
 template <int R, int CW>
 __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0, const double* inv, float* ytiles,
                                             uint32_t* amax, int32_t* exp_s, uint8_t* stages, int stage_bytes,
-                                            int ct) {
+                                            int ct, int64_t row0) {
   const int mode = g.amode;
   const int kTiles = mode == kASilu ? 2 : 1;
   const int w = ct >> 5, lane = ct & 31;
@@ -318,15 +324,30 @@ __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0
     // whole warp, so the shuffles below see every lane.
     constexpr int kRows = (R * kInKernelBlocks + CW - 1) / CW;
     float4 y[kRows];
+    const int64_t kk = k0 + b * kBk + kb;
+    const bool kin = kk < g.k;
 #pragma unroll
     for (int i = 0; i < kRows; ++i) {
       const int r = r0 + i * rstep;
-      y[i] = r < R ? *reinterpret_cast<const float4*>(y_at + r * kBk) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int64_t row = row0 + r;
+      y[i] = (r < R && row < g.m && kin) ? __ldg(reinterpret_cast<const float4*>(g.a + row * g.lda + kk))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    if (mode == kASilu) {
 #pragma unroll
-    for (int i = 0; i < kRows; ++i) {
-      const int r = r0 + i * rstep;
-      if (r < R) y[i] = form(y[i], r);
+      for (int i = 0; i < kRows; ++i) {
+        const int r = r0 + i * rstep;
+        const int64_t row = row0 + r;
+        const float4 u = (r < R && row < g.m && kin) ? __ldg(reinterpret_cast<const float4*>(g.up + row * g.lda + kk))
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        y[i] = make_float4(SiluMul(y[i].x, u.x), SiluMul(y[i].y, u.y), SiluMul(y[i].z, u.z), SiluMul(y[i].w, u.w));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        const int r = r0 + i * rstep;
+        if (r < R) y[i] = form(y[i], r);
+      }
     }
     uint32_t m[kRows];
 #pragma unroll
@@ -480,11 +501,12 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
           TmaLoad3D(stage, &tx, k0, static_cast<int32_t>(row0), 0, &full_x[s]);
         }
       } else {
-        // The fp32 tiles of every k block of the CTA, one barrier per block.
+        // The fp32 tiles of every k block of the CTA, one barrier per block
+        // (64-row tiles; smaller ones are loaded by the converter warps).
         wait_prev();
         float* ytiles = reinterpret_cast<float*>(smem + S * L::kStage);
         const int tiles = g.amode == kASilu ? 2 : 1;
-        for (int i = 0; i < nkb; ++i) {
+        for (int i = 0; i < (R <= 32 ? 0 : nkb); ++i) {  // R <= 32: the converter warps load the rows
           const int32_t k0 = (kb_begin + i) * kBk;
           float* dst = ytiles + i * tiles * R * kBk;
           MbarArriveExpectTx(&full_x[i], static_cast<uint32_t>(tiles * L::kYTile));
@@ -564,9 +586,11 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
         if (ct >= valid && ct < R) inv_s[ct] = 0.0;  // rows past the matrix (their tiles read as zero)
         asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // converter warps only
       }
-      for (int i = 0; i < nkb; ++i) ok &= MbarWaitSleep(&full_x[i], 0);
+      if constexpr (R > 32) {
+        for (int i = 0; i < nkb; ++i) ok &= MbarWaitSleep(&full_x[i], 0);
+      }
       BuildDigits<R, kConvWarps>(g, nkb, static_cast<int64_t>(kb_begin) * kBk, inv_s,
-                        reinterpret_cast<float*>(smem + S * L::kStage), amax_s, exp_s, smem, L::kStage, ct);
+                        reinterpret_cast<float*>(smem + S * L::kStage), amax_s, exp_s, smem, L::kStage, ct, row0);
       FenceProxyAsyncSmem();
       __syncwarp();
       if (lane == 0) MbarArrive(&xready);
