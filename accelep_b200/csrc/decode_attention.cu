@@ -12,7 +12,7 @@
 // context's 64-row chunks are dealt to the S ranks in contiguous ranges. A
 // CTA streams its chunks through two shared-memory buffers with bulk copies
 // (the next chunk is in flight while the current one is scored), keeps an
-// online softmax (running max, sum and weighted values) for the G query heads
+// online softmax (reference maximum, sum and weighted values) for the G query heads
 // of its kv head, and publishes that state in shared memory. The cluster then
 // merges the S states in rank order through distributed shared memory
 // (log-sum-exp rule), so the result does not depend on scheduling and no
@@ -44,6 +44,7 @@ constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxG = 8;        // query heads per kv head
 constexpr int kMaxSplit = 8;    // CTAs per cluster
+constexpr float kSlack = 8.f;   // how far a score may pass a warp's softmax reference before it moves
 constexpr int kChunkFloats = kRows * kD;
 constexpr int kSmemBytes = 2 * 2 * kChunkFloats * 4;  // two buffers of K and V
 
@@ -253,14 +254,21 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
       for (int hh = 0; hh < G; ++hh) {
         const float full_dot = sc[hh] + __shfl_xor_sync(kFull, sc[hh], 1);
         const float x = valid ? full_dot * a.scale : -INFINITY;
-        const float mx = fmaxf(WarpMax(x), m_w[hh]);  // finite: row wr0 < cnt is valid
-        p[hh] = valid ? expf(x - mx) : 0.f;
-        const float sum = WarpSum(half == 0 ? p[hh] : 0.f);
-        const float corr = expf(m_w[hh] - mx);  // 0 on this warp's first rows
-        l_w[hh] = l_w[hh] * corr + sum;
-        m_w[hh] = mx;
-        o[hh][0] *= corr;
-        o[hh][1] *= corr;
+        // The weights are taken against the warp's reference m_w, which moves
+        // to the running maximum only when a score passes it by more than
+        // kSlack (always on the warp's first rows, where m_w is -inf): a
+        // vote instead of a warp maximum per chunk, and no weight above
+        // e^kSlack.
+        if (__any_sync(kFull, x > m_w[hh] + kSlack)) {
+          const float mx = fmaxf(WarpMax(x), m_w[hh]);  // finite: row wr0 < cnt is valid
+          const float corr = expf(m_w[hh] - mx);         // 0 on this warp's first rows
+          l_w[hh] *= corr;
+          o[hh][0] *= corr;
+          o[hh][1] *= corr;
+          m_w[hh] = mx;
+        }
+        p[hh] = valid ? expf(x - m_w[hh]) : 0.f;
+        if (half == 0) l_w[hh] += p[hh];  // this lane's rows; summed over the warp after the loop
       }
       const int rows = min(kWarpRows, cnt - wr0);
       ok &= MbarWait(&full_v[i & 1], (i >> 1) & 1);
@@ -309,6 +317,8 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
     }
   }
   // The four warp states -> one CTA state (log-sum-exp, warps in order).
+#pragma unroll
+  for (int hh = 0; hh < G; ++hh) l_w[hh] = WarpSum(l_w[hh]);
 #pragma unroll
   for (int hh = 0; hh < G; ++hh) {
     wo[warp][hh * kD + 2 * lane] = o[hh][0];

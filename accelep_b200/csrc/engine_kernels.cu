@@ -128,11 +128,33 @@ __global__ void GreedyStepKernel(const float* __restrict__ logits, const int32_t
   } else if (live) {
     const float* row = logits + static_cast<int64_t>(b) * ld;
     Best mine{0.f, -1};
-    for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-      const float v = row[i];
-      if (isnan(v)) continue;
-      if (mine.i < 0 || v > mine.v) mine = Best{v, static_cast<int32_t>(i)};
+    const auto take = [&mine](float v, int64_t i) {
+      if (!isnan(v) && (mine.i < 0 || v > mine.v)) mine = Best{v, static_cast<int32_t>(i)};
+    };
+    int64_t tail = 0;
+    if (ld % 4 == 0 && reinterpret_cast<uintptr_t>(logits) % 16 == 0) {
+      // 16-byte loads, four per thread in flight; a thread's indices rise, so
+      // its first maximum is kept.
+      const float4* row4 = reinterpret_cast<const float4*>(row);
+      const int64_t n4 = vocab / 4, bd = blockDim.x;
+      for (int64_t base = threadIdx.x; base < n4; base += 4 * bd) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          v[u] = base + u * bd < n4 ? __ldg(row4 + base + u * bd) : make_float4(NAN, NAN, NAN, NAN);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t i = 4 * (base + u * bd);
+          take(v[u].x, i);
+          take(v[u].y, i + 1);
+          take(v[u].z, i + 2);
+          take(v[u].w, i + 3);
+        }
+      }
+      tail = 4 * n4;
     }
+    for (int64_t i = tail + threadIdx.x; i < vocab; i += blockDim.x) take(row[i], i);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       Best y{__shfl_xor_sync(kFull, mine.v, o), __shfl_xor_sync(kFull, mine.i, o)};
