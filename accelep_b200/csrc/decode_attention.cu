@@ -277,19 +277,39 @@ __global__ void __launch_bounds__(kThreads, 3) AttnDecodeFusedKernel(FusedArgs a
         for (int hh = 0; hh < G; ++hh) ps[warp][hh][lane >> 1] = p[hh];
       }
       __syncwarp();
-      for (int r4 = 0; r4 < rows; r4 += 4) {
-        float4 pw[G];
+      if (rows == kWarpRows) {
+        // A full chunk: every row's value load can be issued up front.
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) pw[hh] = *reinterpret_cast<const float4*>(&ps[warp][hh][r4]);
+        for (int r4 = 0; r4 < kWarpRows; r4 += 4) {
+          float4 pw[G];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          if (r4 + t < rows) {
+          for (int hh = 0; hh < G; ++hh) pw[hh] = *reinterpret_cast<const float4*>(&ps[warp][hh][r4]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
             const float2 v = *reinterpret_cast<const float2*>(vb + (wr0 + r4 + t) * kD + 2 * lane);
 #pragma unroll
             for (int hh = 0; hh < G; ++hh) {
               const float pr = t == 0 ? pw[hh].x : t == 1 ? pw[hh].y : t == 2 ? pw[hh].z : pw[hh].w;
               o[hh][0] = fmaf(pr, v.x, o[hh][0]);
               o[hh][1] = fmaf(pr, v.y, o[hh][1]);
+            }
+          }
+        }
+      } else {
+        for (int r4 = 0; r4 < rows; r4 += 4) {
+          float4 pw[G];
+#pragma unroll
+          for (int hh = 0; hh < G; ++hh) pw[hh] = *reinterpret_cast<const float4*>(&ps[warp][hh][r4]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            if (r4 + t < rows) {
+              const float2 v = *reinterpret_cast<const float2*>(vb + (wr0 + r4 + t) * kD + 2 * lane);
+#pragma unroll
+              for (int hh = 0; hh < G; ++hh) {
+                const float pr = t == 0 ? pw[hh].x : t == 1 ? pw[hh].y : t == 2 ? pw[hh].z : pw[hh].w;
+                o[hh][0] = fmaf(pr, v.x, o[hh][0]);
+                o[hh][1] = fmaf(pr, v.y, o[hh][1]);
+              }
             }
           }
         }
