@@ -92,8 +92,10 @@ __device__ __forceinline__ float WarpMax(float v) {
 }
 
 // Exact Gelu of the reference (sim_device.cc:239): 0.5 * x * (1 + erf(x / sqrt 2)),
-// every step a rounded float operation.
-__device__ __forceinline__ float GeluExact(float v) {
+// every step a rounded float operation. Not inlined: the epilogues that can
+// apply it are unrolled many times over, and most products never take it
+// (the smaller kernels keep more of their instructions in cache).
+static __device__ __noinline__ float GeluExact(float v) {
   const float e = erff(__fmul_rn(v, 0.7071067811865476f));
   return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.f, e));
 }

@@ -48,15 +48,15 @@ FALLBACK_HBM = 6650.0
 # (profiles/q8_product_decode_qkv_m32.md: per product kind, weighted by the
 # step's launches, 158.0 MB over 121 products; profiles/decode_attention_b32_len1280.md).
 PRODUCT_TRAFFIC = 1_305_636
-ATTENTION_TRAFFIC = 63_622_400
+ATTENTION_TRAFFIC = 63_667_968
 GEMV_TRAFFIC = 274_861_568  # profiles/q8_gemv_c5_m1_k16384.md
 
 
-def config(n):
-    return {"workload": "C4: SmolLM2-135M shape, int8 per-row weights, 32 seqs/GPU x 512-token prompts, greedy "
+def config(n, seqs=SEQS):
+    return {"workload": f"C4: SmolLM2-135M shape, int8 per-row weights, {seqs} seqs/GPU x 512-token prompts, greedy "
                         "decode to 2048 context (1536 new ids per seq); one step = prefill + whole decode",
             "model": "SmolLM2-135M-shaped Llama (30 layers, hidden 576, 9/3 heads, inter 1536, vocab 49152)",
-            "global_batch": SEQS * n, "seq_len": CONTEXT, "prompt_len": PROMPT, "new_tokens_per_seq": NEW,
+            "global_batch": seqs * n, "seq_len": CONTEXT, "prompt_len": PROMPT, "new_tokens_per_seq": NEW,
             "parallelism": f"replicas x{n} (independent sequences, no collective)",
             "l2": "inputs larger than L2: KV cache 3.0 GB and 135 MB of int8 weights per step"}
 
@@ -330,6 +330,7 @@ def attention_roofline(torch, stream, batch=SEQS, length=1280, reps=50):
 
 
 def step_roofline(torch, model, prompts, stream, job_sec, new, peak):
+    seqs = len(prompts)
     """The whole decode step against HBM: the job's time minus its prefill
     (a generate of 0 new ids, timed the same way), per decode step, against
     the bytes one step must move at the job's mean context: the int8 weights
@@ -346,12 +347,12 @@ def step_roofline(torch, model, prompts, stream, job_sec, new, peak):
     step = (job_sec - prefill) / new
     kv_row = 30 * 2 * 3 * 64 * 4  # bytes of one position's keys and values over the 30 layers
     mean_ctx = len(prompts[0]) + (new + 1) / 2.0
-    nbytes = 134_479_872 + 818_688 + SEQS * mean_ctx * kv_row + SEQS * kv_row
+    nbytes = 134_479_872 + 818_688 + seqs * mean_ctx * kv_row + seqs * kv_row
     return {"what": "one C4 decode step (job time minus prefill, / new ids) against the bytes it must move at the "
                     "mean context (weights and scales once, KV rows read, new rows written)",
             "prefill_ms": prefill * 1e3, "decode_step_us": step * 1e6, "bytes_per_step": nbytes,
             "achieved": nbytes / step / 1e9, "peak": peak, "unit": "GB/s", "frac": nbytes / step / 1e9 / peak,
-            "roofline_tok_s": SEQS * peak * 1e9 / nbytes}
+            "roofline_tok_s": seqs * peak * 1e9 / nbytes}
 
 
 def products_roofline(torch, stream, reps=3):
@@ -552,7 +553,10 @@ def run_b200(args):
     del planes, dense
     prompt_len = args.prompt_len or PROMPT
     new = args.new_tokens or NEW
-    prompts = [p[:prompt_len] for p in syn.prompts(cfg, SEQS, max(PROMPT, prompt_len), PROMPT_SEED)]
+    seqs = args.seqs
+    if not 1 <= seqs <= SEQS:
+        raise SystemExit(f"--seqs must be in 1..{SEQS}")
+    prompts = [p[:prompt_len] for p in syn.prompts(cfg, SEQS, max(PROMPT, prompt_len), PROMPT_SEED)][:seqs]
     stream = torch.cuda.ExternalStream(model.stream())
 
     def step():
@@ -594,7 +598,7 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(tensor, op=dist.ReduceOp.MAX)
     dev_sec, wall = float(tensor[0]), float(tensor[1])
-    tokens = SEQS * new * world * args.steps
+    tokens = seqs * new * world * args.steps
     value = tokens / dev_sec
 
     if rank == 0:
@@ -607,15 +611,18 @@ def run_b200(args):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline_one_core()
-        cfg_line = config(world)
+        cfg_line = config(world, seqs)
         if prompt_len != PROMPT or new != NEW:
             cfg_line["workload"] = f"profiling variant: prompt {prompt_len}, {new} new ids (not the C4 bench number)"
+        if seqs != SEQS:
+            cfg_line["workload"] += (f" [{seqs} seqs per GPU: one rank's share of a fixed {SEQS}-sequence batch split "
+                                     f"over {SEQS // seqs} GPUs, not the C4 bench number]")
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": 1000.0 * dev_sec / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 compute",
                 "data": "synthetic (seeded random-init weights and prompts)", "config": cfg_line,
-                "e2e": {"value": tokens / wall, "unit": UNIT, "h2d_bytes_per_step": SEQS * prompt_len * 4,
-                        "d2h_bytes_per_step": SEQS * new * 4},
+                "e2e": {"value": tokens / wall, "unit": UNIT, "h2d_bytes_per_step": seqs * prompt_len * 4,
+                        "d2h_bytes_per_step": seqs * new * 4},
                 "gpu_launches": int(launches),
                 "roofline": {"kernel": "Q8GemmTcKernel: the decode step's 121 int8 products (largest share of the "
                                        "step), graph-replayed, per-launch average", "bound": "hbm",
@@ -657,6 +664,9 @@ def main():
     # Shorter jobs for profiling runs only; a bench number uses the defaults.
     ap.add_argument("--prompt-len", type=int, default=0)
     ap.add_argument("--new-tokens", type=int, default=0)
+    # Sequences per rank (32: the C4 bench). A smaller count measures one
+    # rank's share of a fixed 32-sequence batch split over 32 / seqs GPUs.
+    ap.add_argument("--seqs", type=int, default=SEQS)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
