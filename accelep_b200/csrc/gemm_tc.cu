@@ -235,7 +235,7 @@ __device__ __forceinline__ double RowInverseRms(const float* in, int64_t dim, fl
 // lanes 8q .. 8q + 7, so levels 16 and 8 are shuffles with threads q ^ 2 and
 // q ^ 1 and levels 4, 2, 1 stay inside the thread. dim % 8 == 0.
 template <int R, int CW>
-__device__ __forceinline__ void TileInverseRms(const float* a, int64_t lda, int64_t row0, int valid, int64_t dim,
+__device__ __noinline__ void TileInverseRms(const float* a, int64_t lda, int64_t row0, int valid, int64_t dim,
                                                float eps, int ct, double* inv) {
   for (int base = 0; base < R; base += CW * 8) {
     const int r = base + (ct >> 2), q = ct & 3;
@@ -386,6 +386,81 @@ __device__ __forceinline__ void BuildDigits(const TcArgs& g, int nkb, int64_t k0
 // long weight streams, prefill), which the register budget must allow.
 template <int R, int M>
 constexpr int MinBlocks() { return M != kAPlanes ? 1 : (R == 16 ? 3 : 2); }
+
+// The epilogue of an unsplit tile: rows of the shared-memory tile through the
+// fused epilogue to C (and the peer copies, the row sums). Warp w takes rows
+// w, w + kWarpsN, ...; lane l the columns c4 .. c4 + 3.
+template <int kWarpsN>
+__device__ __forceinline__ void StoreUnsplitBody(const TcArgs& g, const float* tile, int64_t rows, int warp, int lane,
+                                                 int c4, const float (&sc)[4], int64_t cols, int64_t row0,
+                                                 int64_t n0) {
+  if (g.silu_pairs) {
+    for (int r = warp; r < rows; r += kWarpsN) {
+      StoreSiluPairs(g.c, g.ldc, g.vec_store, row0 + r, n0, lane,
+                     *reinterpret_cast<const float4*>(tile + r * kBn + c4), sc);
+    }
+  } else if (g.peers.n == 0 && g.ep.row_sq == nullptr && g.vec_store && cols == kBn) {
+    // The common case, kept free of the optional outputs.
+#pragma unroll 2
+    for (int r = warp; r < rows; r += kWarpsN) {
+      const int64_t row = row0 + r;
+      const float4 v = *reinterpret_cast<const float4*>(tile + r * kBn + c4);
+      *reinterpret_cast<float4*>(g.c + row * g.ldc + n0 + c4) =
+          make_float4(ApplyEpilogue(g.ep, __fmul_rn(v.x, sc[0]), row, n0 + c4),
+                      ApplyEpilogue(g.ep, __fmul_rn(v.y, sc[1]), row, n0 + c4 + 1),
+                      ApplyEpilogue(g.ep, __fmul_rn(v.z, sc[2]), row, n0 + c4 + 2),
+                      ApplyEpilogue(g.ep, __fmul_rn(v.w, sc[3]), row, n0 + c4 + 3));
+    }
+  } else {
+    for (int r = warp; r < rows; r += kWarpsN) {
+      const int64_t row = row0 + r;
+      double sq = 0.0;
+      if (c4 < cols) {
+        const float4 v = *reinterpret_cast<const float4*>(tile + r * kBn + c4);
+        const float in[4] = {v.x, v.y, v.z, v.w};
+        float o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(in[q], sc[q]), row, n0 + c4 + q);
+        if (g.ep.row_sq != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (c4 + q < cols) {
+              const double dv = static_cast<double>(o[q]);
+              sq = fma(dv, dv, sq);  // one fused multiply-add, as every kernel that writes row sums does
+            }
+          }
+        }
+        const int64_t off = row * g.ldc + n0 + c4;
+        if (g.vec_store && c4 + 4 <= cols) {
+          *reinterpret_cast<float4*>(g.c + off) = make_float4(o[0], o[1], o[2], o[3]);
+          StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (c4 + q < cols) {
+              g.c[off + q] = o[q];
+              StorePeers(g.peers, off + q, o[q]);
+            }
+          }
+        }
+      }
+      if (g.ep.row_sq != nullptr) {  // the warp holds the row's columns of this tile
+        sq = WarpSum(sq);
+        if (lane == 0) g.ep.row_sq[row * g.ep.row_sq_ld + n0 / kBn] = sq;
+      }
+    }
+  }
+  if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes
+}
+
+// The same, out of line: the in-kernel (decode) products split K and never
+// take it, and their kernel keeps fewer instructions in cache without it.
+template <int kWarpsN>
+__device__ __noinline__ void StoreUnsplitCold(TcArgs g, const float* tile, int64_t rows, int warp, int lane, int c4,
+                                              float4 scv, int64_t cols, int64_t row0, int64_t n0) {
+  const float sc[4] = {scv.x, scv.y, scv.z, scv.w};
+  StoreUnsplitBody<kWarpsN>(g, tile, rows, warp, lane, c4, sc, cols, row0, n0);
+}
 
 template <int R, int kStagesT, int M>
 __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
@@ -651,65 +726,13 @@ __global__ void __launch_bounds__(Threads<R, M>(), MinBlocks<R, M>())
   if constexpr (!kEarly) load_scales();
   if (splits == 1) {
     if (warp == 1) TmemDealloc(tmem, kCols);
-    // Warp w takes rows w, w + warps, ...; lane l the columns 4l .. 4l + 3.
     if (cta_ok) {
-      if (g.silu_pairs) {
-        for (int r = warp; r < rows; r += kThreads / 32) {
-          StoreSiluPairs(g.c, g.ldc, g.vec_store, row0 + r, n0, lane,
-                         *reinterpret_cast<const float4*>(tile + r * kBn + c4), sc);
-        }
-      } else if (g.peers.n == 0 && g.ep.row_sq == nullptr && g.vec_store && cols == kBn) {
-        // The common case, kept free of the optional outputs.
-#pragma unroll 2
-        for (int r = warp; r < rows; r += kThreads / 32) {
-          const int64_t row = row0 + r;
-          const float4 v = *reinterpret_cast<const float4*>(tile + r * kBn + c4);
-          *reinterpret_cast<float4*>(g.c + row * g.ldc + n0 + c4) =
-              make_float4(ApplyEpilogue(g.ep, __fmul_rn(v.x, sc[0]), row, n0 + c4),
-                          ApplyEpilogue(g.ep, __fmul_rn(v.y, sc[1]), row, n0 + c4 + 1),
-                          ApplyEpilogue(g.ep, __fmul_rn(v.z, sc[2]), row, n0 + c4 + 2),
-                          ApplyEpilogue(g.ep, __fmul_rn(v.w, sc[3]), row, n0 + c4 + 3));
-        }
+      if constexpr (kEarly) {
+        StoreUnsplitCold<kThreads / 32>(g, tile, rows, warp, lane, c4, make_float4(sc[0], sc[1], sc[2], sc[3]), cols,
+                                        row0, n0);
       } else {
-        for (int r = warp; r < rows; r += kThreads / 32) {
-          const int64_t row = row0 + r;
-          double sq = 0.0;
-          if (c4 < cols) {
-            const float4 v = *reinterpret_cast<const float4*>(tile + r * kBn + c4);
-            const float in[4] = {v.x, v.y, v.z, v.w};
-            float o[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) o[q] = ApplyEpilogue(g.ep, __fmul_rn(in[q], sc[q]), row, n0 + c4 + q);
-            if (g.ep.row_sq != nullptr) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (c4 + q < cols) {
-                  const double dv = static_cast<double>(o[q]);
-                  sq = fma(dv, dv, sq);  // one fused multiply-add, as every kernel that writes row sums does
-                }
-              }
-            }
-            const int64_t off = row * g.ldc + n0 + c4;
-            if (g.vec_store && c4 + 4 <= cols) {
-              *reinterpret_cast<float4*>(g.c + off) = make_float4(o[0], o[1], o[2], o[3]);
-              StorePeers4(g.peers, off, make_float4(o[0], o[1], o[2], o[3]));
-            } else {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                if (c4 + q < cols) {
-                  g.c[off + q] = o[q];
-                  StorePeers(g.peers, off + q, o[q]);
-                }
-              }
-            }
-          }
-          if (g.ep.row_sq != nullptr) {  // the warp holds the row's columns of this tile
-            sq = WarpSum(sq);
-            if (lane == 0) g.ep.row_sq[row * g.ep.row_sq_ld + n0 / kBn] = sq;
-          }
-        }
+        StoreUnsplitBody<kThreads / 32>(g, tile, rows, warp, lane, c4, sc, cols, row0, n0);
       }
-      if (g.peers.n > 0) __threadfence_system();  // peer copies land before the kernel completes
     }
     return;
   }
