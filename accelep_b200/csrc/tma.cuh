@@ -94,9 +94,9 @@ __device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete; false when the bound ran out.
-__device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
-  if (MbarTryWait(bar, parity)) return true;
+// The polling loop of MbarWait, out of line: every wait site of a kernel
+// would otherwise carry its own copy of it.
+static __device__ __noinline__ bool MbarWaitPoll(uint64_t* bar, uint32_t parity) {
   const long long start = clock64();
   for (;;) {
     for (int i = 0; i < 256; ++i) {
@@ -104,6 +104,12 @@ __device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
     }
     if (clock64() - start > kWaitLimitCycles) return false;
   }
+}
+
+// Waits for phase `parity` of `bar` to complete; false when the bound ran out.
+__device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity) {
+  if (MbarTryWait(bar, parity)) return true;
+  return MbarWaitPoll(bar, parity);
 }
 
 // The same wait with the suspending try_wait: the thread sleeps inside the
