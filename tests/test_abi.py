@@ -64,6 +64,40 @@ def test_config_struct_layout():
                                                     "context", "eps", "rope_theta"]
 
 
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors of the header's structs have the C compiler's size
+    and field offsets (a field added to one side and not the other shifts
+    what the library reads), and the Python flag constants are the header's."""
+    from accelep_b200 import kernels as K
+    from accelep_b200._lib import Epilogue, L2Prefetch, Q8Plane
+
+    structs = {"accel_b200_epilogue": Epilogue, "accel_b200_l2_prefetch": L2Prefetch,
+               "accel_b200_q8_plane": Q8Plane}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "accel_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", str(src), "-o", str(exe)],
+                   check=True, capture_output=True, text=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        cname, key, value = line.split()
+        got[(cname, key)] = int(value)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert got[(cname, field)] == getattr(py, field).offset, (cname, field)
+    header = (ROOT / "include" / "accel_b200.h").read_text()
+    for name, value in (("ACCEL_B200_EP_TRIGGER_AFTER_WAIT", K.EP_TRIGGER_AFTER_WAIT),
+                        ("ACCEL_B200_ATTN_CACHE_BEFORE_WAIT", K.ATTN_CACHE_BEFORE_WAIT)):
+        assert re.search(rf"#define {name} {value}\b", header), name
+
+
 def test_library_errors_without_device(lib):
     """On a machine without a GPU the library reports an error instead of
     falling back to a CPU path."""
